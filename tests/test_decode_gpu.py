@@ -1,0 +1,219 @@
+"""GPU parity: the sm_100a decode kernel (through the C ABI) against the
+original bytes, the CPU oracle and the reference kernel decode.cu compiled
+unmodified for sm_100a, on the reference's own golden streams, adversarial
+streams and random streams."""
+import ctypes
+import hashlib
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, golden_names, load_golden
+from helpers import random_stream, to_device
+
+pytestmark = pytest.mark.gpu
+GUARD = 0xA5
+
+
+def decode_guarded(d, n, dev, offset=0, misalign=False):
+    """Decodes into the middle of a guard-filled buffer; returns (decoded,
+    guard bytes).  misalign=True shifts every input and the output by one byte
+    so the kernel's unaligned path runs."""
+    from ecf8_b200.run import decode_stream
+    if misalign:  # output_positions must stay 8-byte aligned (the ABI rejects it otherwise)
+        d = {k: (_shift(v) if k in ("encoded", "packed_other_4bits", "gaps") else v) for k, v in d.items()}
+    off = 33 if misalign else 32
+    buf = torch.full((n + 64,), GUARD, dtype=torch.uint8, device=dev)
+    out = buf[off:off + n]
+    decode_stream(d["luts"], d["encoded"], d["packed_other_4bits"], d["output_positions"], d["gaps"], out)
+    torch.cuda.synchronize()
+    b = buf.cpu().numpy()
+    return b[off:off + n], np.concatenate([b[:off], b[off + n:]])
+
+
+def _shift(t):
+    big = torch.empty(t.numel() + 1, dtype=torch.uint8, device=t.device)
+    big[1:] = t
+    return big[1:]
+
+
+def run_reference_kernel(s, dev):
+    """The reference kernel on the same stream (dfloat/run/run.py:97-119
+    geometry).  The LUT buffer is padded to 18 rows and output_positions by
+    one trailing n_elements entry so its reads past the arrays stay inside."""
+    import oracle
+    L = oracle.ref_lib()
+    n = s["packed"].size * 2
+    luts = np.zeros((18, 256), np.uint8)
+    luts[:s["luts"].shape[0]] = s["luts"]
+    op = np.concatenate([s["output_positions"], np.array([n], np.uint64)])
+    t = {"luts": torch.from_numpy(luts).to(dev), "enc": torch.from_numpy(s["encoded"].copy()).to(dev),
+         "packed": torch.from_numpy(s["packed"].copy()).to(dev),
+         "op": torch.from_numpy(op.view(np.int64).copy()).to(dev),
+         "gaps": torch.from_numpy(s["gaps"].copy()).to(dev)}
+    out = torch.zeros(n, dtype=torch.uint8, device=dev)
+    grid = math.ceil(s["encoded"].size / 4096)
+    per = np.diff(s["output_positions"].astype(np.int64))
+    smem = 512 * 4 + 4 + int(per.max() if per.size else 0)
+    st = L.ref_decode_launch(t["luts"].data_ptr(), t["enc"].data_ptr(), t["packed"].data_ptr(),
+                             t["op"].data_ptr(), t["gaps"].data_ptr(), out.data_ptr(),
+                             s["luts"].shape[0], s["encoded"].size, n, grid, 512, smem,
+                             torch.cuda.current_stream().cuda_stream)
+    assert st == 0
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", golden_names())
+@pytest.mark.parametrize("misalign", [False, True])
+def test_golden_streams(cuda_device, oracle_mod, name, misalign):
+    s = load_golden(name)
+    dec, guard = decode_guarded(to_device(s, cuda_device), s["fp8"].size, cuda_device, misalign=misalign)
+    assert np.all(guard == GUARD), "wrote outside outputs[0, n)"
+    assert np.array_equal(dec, s["fp8"])
+    ora, _ = oracle_mod.decode(s)
+    assert np.array_equal(dec, ora)
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_golden_streams_match_reference_kernel(cuda_device, oracle_mod, name):
+    s = load_golden(name)
+    if not oracle_mod.reference_kernel_terminates(s["luts"]):
+        pytest.skip("the reference kernel spins on this stream's EOF bits")
+    ref = run_reference_kernel(s, cuda_device)
+    dec, _ = decode_guarded(to_device(s, cuda_device), s["fp8"].size, cuda_device)
+    assert np.array_equal(ref, s["fp8"])
+    assert np.array_equal(dec, ref)
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_random_streams(cuda_device, oracle_mod, seed):
+    rng = np.random.default_rng(1000 + seed)
+    s = random_stream(oracle_mod, rng)
+    dec, guard = decode_guarded(to_device(s, cuda_device), s["fp8"].size, cuda_device)
+    assert np.all(guard == GUARD)
+    assert np.array_equal(dec, s["fp8"])
+    if seed % 4 == 0:
+        assert np.array_equal(run_reference_kernel(s, cuda_device), dec)
+
+
+def test_batch_of_all_golden_streams(cuda_device):
+    from ecf8_b200.run import decode_streams
+    names = golden_names()
+    ss = [load_golden(n) for n in names]
+    ds = [to_device(s, cuda_device) for s in ss]
+    outs = [torch.zeros(s["fp8"].size, dtype=torch.uint8, device=cuda_device) for s in ss]
+    decode_streams(ds, outs)
+    torch.cuda.synchronize()
+    for n, s, o in zip(names, ss, outs):
+        assert np.array_equal(o.cpu().numpy(), s["fp8"]), n
+
+
+def test_batch_larger_than_one_launch(cuda_device, oracle_mod):
+    from ecf8_b200.run import decode_streams
+    rng = np.random.default_rng(7)
+    ss = [random_stream(oracle_mod, rng, n=int(rng.integers(1, 3000)) * 2) for _ in range(300)]
+    ds = [to_device(s, cuda_device) for s in ss]
+    outs = [torch.zeros(s["fp8"].size, dtype=torch.uint8, device=cuda_device) for s in ss]
+    decode_streams(ds, outs)
+    torch.cuda.synchronize()
+    for s, o in zip(ss, outs):
+        assert np.array_equal(o.cpu().numpy(), s["fp8"])
+
+
+def test_reference_call_convention(cuda_device):
+    """`_decode(grid=, block=, shared_mem=, args=[...])` as compress.py:109-124 calls it."""
+    from ecf8_b200 import _decode
+    s = load_golden("gauss_per_tensor")
+    d = to_device(s, cuda_device)
+    n = s["fp8"].size
+    out = torch.empty(n, dtype=torch.float8_e4m3fn, device=cuda_device)
+    grid = (int(np.ceil(d["encoded"].numel() / (512 * 8))),)
+    _decode(grid=grid, block=(512,), shared_mem=512 * 4 + 4 + 99999,
+            args=[d["luts"].data_ptr(), d["encoded"].data_ptr(), d["packed_other_4bits"].data_ptr(),
+                  d["output_positions"].data_ptr(), d["gaps"].data_ptr(), out.data_ptr(),
+                  d["luts"].shape[0], d["encoded"].numel(), n])
+    torch.cuda.synchronize()
+    assert np.array_equal(out.view(torch.uint8).cpu().numpy(), s["fp8"])
+
+
+def test_repeat_decode_is_idempotent(cuda_device):
+    s = load_golden("fibonacci_depth16")
+    d = to_device(s, cuda_device)
+    a, _ = decode_guarded(d, s["fp8"].size, cuda_device)
+    b, _ = decode_guarded(d, s["fp8"].size, cuda_device)
+    assert np.array_equal(a, b)
+
+
+def test_corrupt_streams_stay_in_bounds(cuda_device):
+    """Garbage gaps / output positions / LUTs must not make the kernel touch
+    memory outside the buffers it was given (unspecified bytes inside)."""
+    rng = np.random.default_rng(3)
+    s = load_golden("gauss_block128")
+    n = s["fp8"].size
+    for trial in range(6):
+        c = {k: v.copy() for k, v in s.items()}
+        if trial % 3 == 0:
+            c["gaps"] = rng.integers(0, 256, c["gaps"].size).astype(np.uint8)
+        elif trial % 3 == 1:
+            c["output_positions"] = rng.integers(0, 2 * n, c["output_positions"].size).astype(np.uint64)
+        else:
+            c["luts"] = rng.integers(0, 256, c["luts"].shape).astype(np.uint8)
+        _, guard = decode_guarded(to_device(c, cuda_device), n, cuda_device)
+        assert np.all(guard == GUARD)
+
+
+def _quantize_block128(w):
+    o, i = w.shape
+    t = w.reshape(o // 128, 128, i // 128, 128)
+    amax = t.abs().amax(dim=(1, 3), keepdim=True).clamp(min=1e-12)
+    return (t * (448.0 / amax)).to(torch.float8_e4m3fn).reshape(o, i)
+
+
+def test_config1_on_gpu_matches_reference_digests(cuda_device):
+    """Config 1 through the GPU packer with the reference's code table: every
+    buffer hashes like the reference packer's, and decodes back exactly."""
+    from ecf8_b200 import codec
+    from ecf8_b200.run import decode_stream
+    meta = json.load(open(os.path.join(GOLDEN, "config1_digests.json")))
+    w = torch.randn(4096, 4096, generator=torch.Generator().manual_seed(0)) * 0.02
+    fp8 = (w * (448.0 / w.abs().max())).to(torch.float8_e4m3fn).flatten().to(cuda_device)
+    exps, packed = codec.get_exponents_and_other_4bits_fp8_e4m3(fp8)
+    table = {int(a): (int(b), int(c)) for a, b, c in
+             zip(meta["table_symbols"], meta["table_bits"], meta["table_values"])}
+    table[codec.EOF] = (meta["eof_bits"], meta["eof_value"])
+    enc, gaps, op = codec.encode_exponents_for_cuda(exps, codec.HuffmanCode(table))
+    luts = codec.get_luts_from_huffman_table(table).to(cuda_device)
+    sha = lambda t: hashlib.sha256(t.contiguous().view(torch.uint8).cpu().numpy().tobytes()).hexdigest()
+    assert sha(enc) == meta["sha256"]["encoded"]
+    assert sha(gaps) == meta["sha256"]["gaps"]
+    assert sha(op) == meta["sha256"]["output_positions"]
+    assert sha(packed) == meta["sha256"]["packed"]
+    out = decode_stream(luts, enc, packed.contiguous(), op, gaps)
+    assert torch.equal(out.view(torch.uint8), fp8.view(torch.uint8))
+
+
+def test_full_qwen3_8b_layer_round_trip(cuda_device):
+    """One Qwen3-8B-shaped layer stream (192,937,984 elements, 128x128 block
+    scales, sub-Linears in sorted-name order): GPU encode -> decode is the
+    identity, and a second decode into the same scratch gives the same bytes."""
+    from ecf8_b200.codec import compress_fp8
+    from ecf8_b200.run import decode_stream
+    shapes = [("mlp.down_proj", 4096, 12288), ("mlp.gate_proj", 12288, 4096), ("mlp.up_proj", 12288, 4096),
+              ("self_attn.k_proj", 1024, 4096), ("self_attn.o_proj", 4096, 4096),
+              ("self_attn.q_proj", 4096, 4096), ("self_attn.v_proj", 1024, 4096)]
+    g = torch.Generator(device=cuda_device).manual_seed(0)
+    flat = torch.cat([_quantize_block128(torch.randn(o, i, generator=g, device=cuda_device) * 0.02).reshape(-1)
+                      for _, o, i in shapes])
+    assert flat.numel() == 192_937_984
+    c = compress_fp8(flat)
+    assert 2.4 < c["entropy"] < 2.8
+    out = decode_stream(c["luts"], c["encoded"], c["packed_other_4bits"], c["output_positions"], c["gaps"])
+    assert torch.equal(out.view(torch.uint8), flat.view(torch.uint8))
+    out2 = decode_stream(c["luts"], c["encoded"], c["packed_other_4bits"], c["output_positions"], c["gaps"],
+                         out)
+    assert torch.equal(out2.view(torch.uint8), flat.view(torch.uint8))

@@ -1,0 +1,102 @@
+"""Decode-before-forward hook end to end: a model whose FP8 blocks are saved
+as ECF8 streams, loaded through the loader, gives bit-identical outputs to the
+uncompressed model, and all blocks share one per-device scratch buffer."""
+import json
+import os
+
+import pytest
+import torch
+import torch.nn as nn
+
+pytestmark = pytest.mark.gpu
+
+
+class FP8Linear(nn.Module):
+    """y = x @ (w_fp8 * scale)^T, computed in fp32 (stands in for the model's FP8 matmul)."""
+
+    def __init__(self, i, o, gen, dev):
+        super().__init__()
+        self.in_features, self.out_features = i, o
+        w = torch.randn(o, i, generator=gen, device=dev) * 0.02
+        s = 448.0 / w.abs().max()
+        self.weight = nn.Parameter((w * s).to(torch.float8_e4m3fn), requires_grad=False)
+        self.register_buffer("weight_scale_inv", (1.0 / s).reshape(1))
+
+    def forward(self, x):
+        return x @ (self.weight.float() * self.weight_scale_inv).t()
+
+
+class Block(nn.Module):
+    def __init__(self, h, f, gen, dev):
+        super().__init__()
+        self.down_proj = FP8Linear(f, h, gen, dev)
+        self.gate_proj = FP8Linear(h, f, gen, dev)
+        self.up_proj = FP8Linear(h, f, gen, dev)
+
+    def forward(self, x):
+        return x + self.down_proj(torch.nn.functional.silu(self.gate_proj(x)) * self.up_proj(x))
+
+
+class Tiny(nn.Module):
+    def __init__(self, dev, seed=0, n=3, h=256, f=512):
+        super().__init__()
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.layers = nn.ModuleList([Block(h, f, g, dev) for _ in range(n)])
+
+    def forward(self, x):
+        for layer in self.layers:
+            x = layer(x)
+        return x
+
+
+def save_compressed(model, path):
+    """Writes the reference on-disk layout: one safetensors file holding, per
+    block, luts / encoded / packed_other_4bits / output_positions (as bytes) /
+    gaps / split_positions, plus pattern_dict.json (compress.py:587-680)."""
+    from safetensors.torch import save_file
+    from ecf8_b200.codec import compress_fp8
+    tensors = {}
+    names = ["down_proj", "gate_proj", "up_proj"]
+    for i, blk in enumerate(model.layers):
+        ws = [getattr(blk, n).weight.data.reshape(-1) for n in names]
+        flat = torch.cat(ws)
+        c = compress_fp8(flat)
+        pre = f"layers.{i}."
+        tensors[pre + "luts"] = c["luts"].cpu()
+        tensors[pre + "encoded"] = c["encoded"].cpu()
+        tensors[pre + "packed_other_4bits"] = c["packed_other_4bits"].cpu()
+        tensors[pre + "output_positions"] = c["output_positions"].view(torch.uint8).cpu()
+        tensors[pre + "gaps"] = c["gaps"].cpu()
+        tensors[pre + "split_positions"] = torch.cumsum(torch.tensor([w.numel() for w in ws]), 0)[:-1]
+        for n in names:
+            tensors[pre + n + ".weight_scale_inv"] = getattr(blk, n).weight_scale_inv.cpu()
+    save_file(tensors, os.path.join(path, "model.safetensors"))
+    with open(os.path.join(path, "pattern_dict.json"), "w") as f:
+        json.dump({"fp8": {r"layers\.\d+": names}, "bf16": {}}, f)
+
+
+@pytest.mark.parametrize("parallel", [False, True])
+def test_hooked_model_matches_uncompressed(cuda_device, tmp_path, parallel):
+    from ecf8_b200 import load_and_replace_tensors, load_and_replace_tensors_parallel
+    from ecf8_b200.run import TensorManager
+    dev = cuda_device
+    ref = Tiny(dev)
+    x = torch.randn(8, 256, device=dev)
+    y_ref = ref(x)
+    save_compressed(ref, str(tmp_path))
+    model = Tiny(dev, seed=123)  # different weights: must be replaced by the streams
+    cfg = {"threads_per_block": 512, "bytes_per_thread": 8,
+           "pattern_dict": json.load(open(tmp_path / "pattern_dict.json"))}
+    loader = load_and_replace_tensors_parallel if parallel else load_and_replace_tensors
+    loader(model, str(tmp_path), cfg)
+    for blk in model.layers:
+        assert "weight" not in blk.down_proj._parameters
+    model.to(dev)
+    TensorManager.clear_device()
+    y = model(x)
+    torch.cuda.synchronize()
+    assert torch.equal(y, y_ref)
+    # every block decoded into the same per-device scratch
+    ptrs = {blk.down_proj.weight.data_ptr() for blk in model.layers}
+    assert len(ptrs) == 1
+    assert TensorManager._tensors[dev].numel() == 3 * 256 * 512
