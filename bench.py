@@ -190,11 +190,11 @@ def barrier(world):
 # Our arm
 # ---------------------------------------------------------------------------
 
-def build_qwen3_8b(dev):
+def build_qwen3_8b(dev, n_layers=QWEN3_8B_LAYERS):
     from ecf8_b200.codec import compress_fp8
     layers, originals = [], []
     t0 = time.time()
-    for l in range(QWEN3_8B_LAYERS):
+    for l in range(n_layers):
         flat = make_stream_weights(QWEN3_8B_LINEARS, l * 7, dev)
         c = compress_fp8(flat)
         layers.append(c)
@@ -234,7 +234,7 @@ def run_ours(args, rank, world, dev):
     L = _lib.lib()
     stream = torch.cuda.current_stream(dev)
     if world == 1:
-        layers, originals = build_qwen3_8b(dev)
+        layers, originals = build_qwen3_8b(dev, args.layers)
         n_max = max(c["packed_other_4bits"].numel() * 2 for c in layers)
         scratch = TensorManager.get_tensor(dev, n_max).view(torch.uint8)
         calls = [decode_args(L, c, scratch, stream) for c in layers]
@@ -323,14 +323,14 @@ def run_ours(args, rank, world, dev):
 
     # end to end through the host-buffer API: pinned host in, decode, pinned host out
     e2e = None
-    if world == 1:
+    if world == 1 and not args.no_e2e:
         e2e = run_e2e(args, layers, originals[-1], dev)
 
     cpu = cpu_baseline(layers[0]) if (world == 1 and rank == 0 and not args.no_cpu_baseline) else None
     if rank != 0:
         return None
     cfg = {
-        "workload": ("config 2: Qwen3-8B-shaped FP8 weight set decode, 36 layer streams x 192,937,984 "
+        "workload": (f"config 2: Qwen3-8B-shaped FP8 weight set decode, {len(layers)} layer streams x 192,937,984 "
                      "e4m3 weights, one launch per layer into the shared scratch" if world == 1 else
                      f"config 5: Qwen3-235B-A22B-shaped MoE decode, {args.moe_layers} layers, 128 experts "
                      f"x 18,874,368 weights split {QWEN3_235B_EXPERTS // world}/GPU + attention replica "
@@ -575,6 +575,9 @@ def main():
     ap.add_argument("--moe-layers", type=int, default=QWEN3_235B_LAYERS)
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--layers", type=int, default=QWEN3_8B_LAYERS,
+                    help="config-2 layers to build (fewer only for profiling a small case)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

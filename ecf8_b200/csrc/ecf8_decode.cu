@@ -38,6 +38,7 @@ namespace {
 
 constexpr int kThreads = ECF8_THREADS_PER_BLOCK;        // windows per group
 constexpr int kWindowBytes = ECF8_BYTES_PER_THREAD;     // bytes per window
+constexpr int kGroupBytes = kThreads * kWindowBytes;    // 4096
 constexpr int kTabBits = 12;                            // multi-symbol table width
 constexpr int kTabSize = 1 << kTabBits;
 constexpr int kMaxSymsPerEntry = 5;                     // 5 nibbles fit in bits 31..12
@@ -45,18 +46,26 @@ constexpr int kSlotWords = 9;                           // 72 nibbles >= 64 + 4 
 constexpr int kMaxGroupElems = kThreads * 64;           // one symbol per bit at most
 constexpr int kObufWords = (kMaxGroupElems + 32) / 8;   // + 15 head pad, round to 16
 constexpr int kLutRows = ECF8_MAX_LUTS - 1;             // decode rows (row 0 + prefixes)
+constexpr int kEncStage = kGroupBytes + 16;             // group bytes + look-ahead, 16-byte units
+constexpr int kGapStage = kThreads / 2;                 // 4 bits per window
+constexpr int kPackStage = kMaxGroupElems / 2 + 32;     // packed nibbles of one group (+ alignment)
 
 struct alignas(16) Smem {
     uint32_t tab[kTabSize];                  // multi-symbol entries
     uint32_t slot[kThreads * kSlotWords];    // per-window decoded nibbles (MSB first)
     uint32_t obuf[kObufWords];               // output-ordered exponent nibbles
-    uint16_t tmask[kTabSize];                // start offsets of the symbols of an entry
+    uint8_t enc[2][kEncStage];               // staged bitstream, double buffered
+    uint8_t gaps[2][kGapStage];              // staged gaps, double buffered
+    uint8_t pack[kPackStage];                // staged sign+mantissa nibbles
+    uint16_t tmask[kTabSize + 8];            // start offsets of an entry's symbols (+ sentinel)
     uint8_t lut[kLutRows * 256];             // reference LUT rows 0..n_luts-2, zero padded
     uint8_t lens[256];                       // reference LUT last row: code lengths
     uint32_t chg[kLutRows * 8];              // per row: bit b set if entry b != entry b-1
     uint32_t wsum[kThreads / 32];            // block-scan warp totals
 };
 static_assert(offsetof(Smem, obuf) % 16 == 0, "obuf must allow 8-byte vector reads");
+static_assert(offsetof(Smem, enc) % 16 == 0 && kEncStage % 16 == 0, "cp.async targets are 16-byte units");
+static_assert(offsetof(Smem, gaps) % 16 == 0 && offsetof(Smem, pack) % 16 == 0, "cp.async alignment");
 
 struct DevStream {
     const uint8_t* luts;
@@ -71,8 +80,8 @@ struct DevStream {
     long long group_begin;  // first global work index of this stream
     int n_groups;
     int n_luts;
-    int vec_ok;             // encoded/packed 8-byte and out 16-byte aligned
-    int pad_;
+    int async_ok;           // encoded, packed and gaps 16-byte aligned: cp.async staging
+    int out16;              // outputs 16-byte aligned: 16-byte stores
 };
 
 template <int MAXS>
@@ -84,11 +93,41 @@ struct Batch {
 };
 
 // ---------------------------------------------------------------------------
+// Staging: global -> shared copies of 16-byte units, zero-filled past `limit`.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t bytes) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+// Copies bytes [lo, lo + size) of `src` (valid below `limit`) to dst[0, size);
+// size is a multiple of 16.  Asynchronous with cp.async when src + lo is
+// 16-byte aligned, else plain byte loads.
+__device__ __forceinline__ void stage(uint8_t* dst, const uint8_t* src, long long lo, int size, long long limit,
+                                      bool async_ok) {
+    for (int i = threadIdx.x * 16; i < size; i += kThreads * 16) {
+        const long long a = lo + i;
+        long long v = limit - a;
+        v = v < 0 ? 0 : (v > 16 ? 16 : v);
+        if (async_ok) {
+            cp_async16(dst + i, v ? src + a : src, (uint32_t)v);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) dst[i + k] = k < v ? __ldg(src + a + k) : (uint8_t)0;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Per-stream set-up: copy the reference LUTs and derive the multi-symbol table.
 // Entry layout (u32): bits 31..12 up to five 4-bit symbols, first symbol in
 // the top nibble; bits 11..8 the number of stream bits the symbols use; bits
 // 4..0 four times the symbol count (so the entry is directly a funnel-shift
-// amount).  An entry with count 0 means the first code is longer than 12 bits.
+// amount).  An all-zero entry means no complete code starts the pattern
+// within 12 bits; the decoder then uses the two-level LUT directly.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t lut_symbol(const Smem& S, uint32_t top) {
     // `top` holds the next >= 16 stream bits left-aligned (dfloat/run/decode.cu:86-88).
@@ -105,8 +144,7 @@ __device__ __forceinline__ uint32_t code_length(const Smem& S, uint32_t sym) {
 }
 
 // True when LUT row `row` holds one value over the 2^pad entries starting at
-// `lo` (lo is a multiple of 2^pad).  A lookup whose key has only its top
-// 8 - pad bits known is decided iff this holds.
+// `lo` (lo is a multiple of 2^pad).
 __device__ __forceinline__ bool row_constant(const Smem& S, int row, uint32_t lo, uint32_t pad) {
     if (pad == 0) return true;
     const uint32_t* c = S.chg + row * 8;
@@ -119,13 +157,40 @@ __device__ __forceinline__ bool row_constant(const Smem& S, int row, uint32_t lo
     return acc == 0;
 }
 
+// The code at the top of the 16-bit value v, if it is a real code: one whose
+// whole code range maps to it in the LUTs.  Every code of the table is one;
+// bit patterns of the EOF code or of unused code space are not (there the
+// LUT's carry-forward answer depends on bits past the returned length).
+__device__ __forceinline__ bool real_code(const Smem& S, uint32_t v, uint32_t& sym, uint32_t& len) {
+    const uint32_t b1 = v >> 8;
+    const uint32_t d = S.lut[b1];
+    if (d < 240) {
+        const uint32_t l = S.lens[d];
+        if (l == 0 || l > 8) return false;
+        if (!row_constant(S, 0, b1 & ~((1u << (8 - l)) - 1u), 8 - l)) return false;
+        sym = d;
+        len = l;
+        return true;
+    }
+    const int row = 256 - (int)d;
+    const uint32_t b2 = v & 255u;
+    const uint32_t d2 = S.lut[row * 256 + b2];
+    const uint32_t l = S.lens[d2 & 255u];
+    if (l <= 8 || l > 16) return false;
+    if (!row_constant(S, row, b2 & ~((1u << (16 - l)) - 1u), 16 - l)) return false;
+    sym = d2;
+    len = l;
+    return true;
+}
+
 __device__ void build_tables(Smem& S, const DevStream& d) {
     const int t = threadIdx.x;
     for (int i = t; i < kLutRows * 256; i += kThreads) {
-        int row = i >> 8;
+        const int row = i >> 8;
         S.lut[i] = (row < d.n_luts - 1) ? __ldg(d.luts + i) : (uint8_t)0;
     }
     for (int i = t; i < 256; i += kThreads) S.lens[i] = __ldg(d.luts + (d.n_luts - 1) * 256 + i);
+    if (t < 8) S.tmask[kTabSize + t] = 1;  // start mask of a single directly decoded code
     __syncthreads();
     // Change bitmaps, one ballot per 32 entries (rows are 256 = 8 x 32 wide).
     for (int i = t; i < kLutRows * 256; i += kThreads) {
@@ -134,112 +199,95 @@ __device__ void build_tables(Smem& S, const DevStream& d) {
         if ((t & 31) == 0) S.chg[i >> 5] = m;
     }
     __syncthreads();
-    // Multi-symbol entries.  The pattern's 12 bits are followed by unknown
-    // bits; a symbol is taken only if every continuation of the known bits
-    // gives the same LUT result (carry-forward entries can otherwise map
-    // padding to a code that does not match the bits) and its code fits.
-    for (int x = t; x < kTabSize; x += kThreads) {
-        const uint32_t v = (uint32_t)x << (32 - kTabBits);
-        uint32_t syms = 0, mask = 0, pos = 0, c = 0;
-        while (c < (uint32_t)kMaxSymsPerEntry) {
-            const uint32_t u = v << pos;
-            const uint32_t avail = kTabBits - pos;
-            const uint32_t b1 = u >> 24;
-            if (!row_constant(S, 0, b1, 8 - min(8u, avail))) break;
-            uint32_t sym = S.lut[b1];
-            if (sym >= 240) {
-                const int row = 256 - (int)sym;
-                const uint32_t b2 = (u >> 16) & 255u;
-                if (!row_constant(S, row, b2, 8 - (avail > 8 ? avail - 8 : 0))) break;
-                sym = S.lut[row * 256 + b2];
-            }
-            const uint32_t len = code_length(S, sym);
-            if (pos + len > (uint32_t)kTabBits) break;
+    // Entry 0 (all-zero pattern) greedily.
+    if (t == 0) {
+        uint32_t syms = 0, mask = 0, pos = 0, c = 0, sym, len;
+        while (c < (uint32_t)kMaxSymsPerEntry && real_code(S, 0, sym, len) && pos + len <= (uint32_t)kTabBits) {
             syms |= (sym & 15u) << (28 - 4 * c);
             mask |= 1u << pos;
             pos += len;
             ++c;
         }
-        S.tab[x] = syms | (pos << 8) | (4 * c);
-        S.tmask[x] = (uint16_t)mask;
+        S.tab[0] = syms | (pos << 8) | (4 * c);
+        S.tmask[0] = (uint16_t)mask;
+    }
+    __syncthreads();
+    // Entry x from entry y = (x << l) & 0xfff, where l is x's first code length:
+    // y's codes that end within the remaining 12 - l bits follow.  y has more
+    // trailing zeros than x, so entries are built in order of decreasing
+    // trailing-zero count, one round per count.
+    for (int tz = kTabBits - 1; tz >= 0; --tz) {
+        const int n = 1 << (kTabBits - 1 - tz);
+        for (int j = t; j < n; j += kThreads) {
+            const uint32_t x = (uint32_t)(2 * j + 1) << tz;
+            uint32_t sym, len, ent = 0, msk = 0;
+            if (real_code(S, x << 4, sym, len) && len <= (uint32_t)kTabBits) {
+                uint32_t kept = 0, endk = 0, rest = 0, mrest = 0;
+                if (len < (uint32_t)kTabBits) {
+                    const uint32_t y = (x << len) & (kTabSize - 1);
+                    const uint32_t ey = S.tab[y], my = S.tmask[y];
+                    const uint32_t endmask = (ey & 31u) ? ((my & ~1u) | (1u << ((ey >> 8) & 15u))) : 0u;
+                    kept = min(__popc(endmask & ((2u << (kTabBits - len)) - 1u)), kMaxSymsPerEntry - 1);
+                    if (kept) {
+                        endk = __fns(endmask, 0, (int)kept);
+                        rest = (ey >> 4) & (((1u << (4 * kept)) - 1u) << (28 - 4 * kept));
+                        mrest = my & ((1u << endk) - 1u);
+                    }
+                }
+                ent = ((sym & 15u) << 28) | rest | ((len + endk) << 8) | (4 * (1 + kept));
+                msk = 1u | (mrest << len);
+            }
+            S.tab[x] = ent;
+            S.tmask[x] = (uint16_t)msk;
+        }
+        __syncthreads();
     }
 }
 
 // ---------------------------------------------------------------------------
-// Window decode.  The 64 window bits plus 16 look-ahead bits are kept in a
-// left-aligned 64-bit shift register (hi:lo); p is the window bit offset of
-// its top.  Decoded nibbles go through a 64-bit accumulator (ah:al) into the
-// thread's shared-memory slot, eight at a time.
+// Window decode.  Stream bits [p, 80) of the window (64 bits + 16 look-ahead)
+// sit left-aligned in the 96-bit shift register (h:m:x).  Decoded nibbles go
+// through a 64-bit accumulator (ah:al) into the thread's shared-memory slot,
+// eight at a time.  Returns the number of codes that start in bits [gap, 64)
+// (decode.cu:65-112).
 // ---------------------------------------------------------------------------
-struct Decoder {
-    uint32_t hi, lo;       // bit register
-    uint32_t ah, al;       // nibble accumulator (newest nibble in the low bits)
-    uint32_t n4;           // 4 x symbols appended
-    uint32_t m4;           // 4 x symbols not yet spilled
-    uint32_t* slot;
-    int k;                 // words spilled
-    int p;                 // window bit offset of the register's top bit
-    uint32_t last_idx;     // table index of the last table step
-    int last_p;            // window offset of the last step
-    bool last_table;       // whether the last step used the table
-
-    __device__ __forceinline__ void step(const Smem& S) {
-        const uint32_t idx = hi >> (32 - kTabBits);
-        uint32_t e = S.tab[idx];
-        uint32_t b = (e >> 8) & 15u;
-        last_idx = idx;
-        last_p = p;
-        last_table = (e & 31u) != 0;
-        if (!last_table) {  // first code longer than the table width
-            const uint32_t sym = lut_symbol(S, hi);
+__device__ __forceinline__ uint32_t decode_window(const Smem& S, uint32_t* slot, uint32_t w0, uint32_t w1,
+                                                  uint32_t la, uint32_t gap) {
+    uint32_t h = __funnelshift_l(w1, w0, gap);
+    uint32_t m = __funnelshift_l(la << 16, w1, gap);
+    uint32_t x = (la << 16) << gap;
+    uint32_t p = gap, ah = 0, al = 0, m4 = 0;
+    uint32_t* sp = slot;
+    uint32_t idx, e, b;
+    do {
+        idx = h >> (32 - kTabBits);
+        e = S.tab[idx];
+        b = (e >> 8) & 15u;
+        if (b == 0) {  // no complete code within the table width: two-level LUT
+            const uint32_t sym = lut_symbol(S, h);
             b = code_length(S, sym);
             e = ((sym & 15u) << 28) | 4u;
+            idx = kTabSize;
         }
-        // append the entry's symbols: shift amount = e & 31 = 4 x count
-        ah = __funnelshift_l(al, ah, e);
+        ah = __funnelshift_l(al, ah, e);  // append e's symbols; shift = e & 31 = 4 x count
         al = __funnelshift_l(e, al, e);
-        n4 += e & 31u;
         m4 += e & 31u;
         if (m4 >= 32) {
             m4 -= 32;
-            slot[k++] = __funnelshift_r(al, ah, m4);
+            *sp++ = __funnelshift_r(al, ah, m4);
         }
-        hi = __funnelshift_l(lo, hi, b);
-        lo <<= b;
-        p += (int)b;
-    }
-};
-
-// Decodes the codes that start in window bits [gap, 64) (decode.cu:65-112) and
-// returns how many there are; their nibbles are in `slot`.
-__device__ __forceinline__ uint32_t decode_window(const Smem& S, uint32_t* slot, uint32_t whi,
-                                                  uint32_t wlo, uint32_t la, int gap) {
-    Decoder D;
-    D.hi = __funnelshift_l(wlo, whi, gap);
-    D.lo = wlo << gap;
-    D.ah = D.al = 0;
-    D.n4 = D.m4 = 0;
-    D.slot = slot;
-    D.k = 0;
-    D.p = gap;
-    D.last_idx = 0;
-    D.last_p = 0;
-    D.last_table = false;
-    while (D.p < 16) D.step(S);
-    // The register's low p bits are empty: the 16 look-ahead bits go right
-    // below the remaining window bits (decode.cu:100).
-    D.lo |= la << (D.p - 16);
-    while (D.p < 64) D.step(S);
-    if (D.m4) slot[D.k] = D.al << (32 - D.m4);
-    uint32_t n = D.n4 >> 2;
-    // The last table step may have taken symbols that start at or after bit
-    // 64; they belong to the next window.
-    const int room = 64 - D.last_p;
-    if (D.last_table && room < kTabBits) {
-        const uint32_t e = S.tab[D.last_idx];
-        const uint32_t keep = __popc((uint32_t)S.tmask[D.last_idx] & ((1u << room) - 1u));
-        n -= ((e & 31u) >> 2) - keep;
-    }
+        h = __funnelshift_l(m, h, b);
+        m = __funnelshift_l(x, m, b);
+        x <<= b;
+        p += b;
+    } while (p < 64);
+    if (m4) *sp = al << (32 - m4);
+    uint32_t n = (uint32_t)(sp - slot) * 8 + (m4 >> 2);
+    // The last step may have taken codes that start at or after bit 64; they
+    // belong to the next window.
+    const uint32_t room = 64 - (p - b);
+    if (room < (uint32_t)kTabBits)
+        n -= ((e & 31u) >> 2) - __popc((uint32_t)S.tmask[idx] & ((1u << room) - 1u));
     return n;
 }
 
@@ -253,138 +301,160 @@ __device__ __forceinline__ void merge8(uint32_t ew, uint32_t pw, uint32_t& lo, u
     hi = __byte_perm(ev, od, 0x7362);
 }
 
-__device__ __forceinline__ uint8_t merge1(const Smem& S, const DevStream& d,
-                                          unsigned long long base, unsigned long long i) {
-    const uint32_t rel = (uint32_t)(i - base);
-    const uint32_t e = (S.obuf[rel >> 3] >> (28 - 4 * (rel & 7))) & 15u;
-    const uint32_t pb = __ldg(d.packed + (i >> 1));
-    const uint32_t n = (i & 1) ? (pb & 15u) : (pb >> 4);
-    return (uint8_t)((e << 3) | ((n & 8u) << 4) | (n & 7u));
-}
+// Output range of group g: [output_positions[g], output_positions[g+1])
+// (decode.cu:116,144-145,208), an entry the array lacks counting as n_elements.
+struct GroupRange {
+    unsigned long long start, end;
+};
 
-__device__ void decode_group(Smem& S, const DevStream& d, long long g) {
-    const int t = threadIdx.x;
+__device__ __forceinline__ GroupRange group_range(const DevStream& d, long long g) {
     const unsigned long long N = (unsigned long long)d.n_elements;
-    // Group g places elements [output_positions[g], output_positions[g+1])
-    // (decode.cu:116,144-145,208); an entry the array lacks counts as N.
-    unsigned long long start = (g < d.n_op) ? d.op[g] : N;
-    unsigned long long end = (g + 1 < d.n_op) ? d.op[g + 1] : N;
+    unsigned long long start = (g < d.n_op) ? __ldg(d.op + g) : N;
+    unsigned long long end = (g + 1 < d.n_op) ? __ldg(d.op + g + 1) : N;
     if (end > N) end = N;
     if (start > end) start = end;
     if (end - start > (unsigned long long)kMaxGroupElems) end = start + kMaxGroupElems;
-    const unsigned long long base = start & ~15ull;
-    const int n_chunks = (int)((end - base + 15) >> 4);
-    for (int i = t; i < 2 * n_chunks; i += kThreads) S.obuf[i] = 0;
+    return {start, end};
+}
 
-    // --- window load (decode.cu:42-62) ---
-    const long long wi = g * kThreads + t;
-    const long long wb = wi * kWindowBytes;
-    uint32_t* slot = S.slot + t * kSlotWords;
-    uint32_t count = 0;
-    if (wb < d.n_bytes) {
-        uint32_t whi, wlo, la;
-        if (d.vec_ok && wb + kWindowBytes + 2 <= d.n_bytes) {
-            const uint2 raw = __ldg(reinterpret_cast<const uint2*>(d.encoded + wb));
-            const uint32_t r16 = __ldg(reinterpret_cast<const unsigned short*>(d.encoded + wb + 8));
-            whi = __byte_perm(raw.x, 0, 0x0123);
-            wlo = __byte_perm(raw.y, 0, 0x0123);
-            la = ((r16 & 0xffu) << 8) | (r16 >> 8);
-        } else {
-            uint32_t b[10];
-#pragma unroll
-            for (int i = 0; i < 10; ++i) b[i] = (wb + i < d.n_bytes) ? __ldg(d.encoded + wb + i) : 0u;
-            whi = (b[0] << 24) | (b[1] << 16) | (b[2] << 8) | b[3];
-            wlo = (b[4] << 24) | (b[5] << 16) | (b[6] << 8) | b[7];
-            la = (b[8] << 8) | b[9];
-        }
-        const uint32_t gb = __ldg(d.gaps + (wi >> 1));
-        const int gap = (int)((wi & 1) ? (gb & 15u) : (gb >> 4));
-        count = decode_window(S, slot, whi, wlo, la, gap);
-    }
-    // Windows that lie wholly past n_bytes only follow the last real code, so
-    // they place nothing; they count 0.
+__device__ __forceinline__ void stage_window_bytes(Smem& S, int buf, const DevStream& d, long long g) {
+    stage(S.enc[buf], d.encoded, g * kGroupBytes, kEncStage, d.n_bytes, d.async_ok);
+    stage(S.gaps[buf], d.gaps, g * kGapStage, kGapStage, g * kGapStage + kGapStage, d.async_ok);
+}
 
-    // --- block exclusive scan of window counts (decode.cu:114-148) ---
-    const int lane = t & 31, warp = t >> 5;
-    uint32_t v = count;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t n = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += n;
-    }
-    if (lane == 31) S.wsum[warp] = v;
-    __syncthreads();
-    if (warp == 0) {
-        uint32_t s = lane < kThreads / 32 ? S.wsum[lane] : 0u;
-#pragma unroll
-        for (int o = 1; o < kThreads / 32; o <<= 1) {
-            const uint32_t n = __shfl_up_sync(0xffffffffu, s, o);
-            if (lane >= o) s += n;
-        }
-        if (lane < kThreads / 32) S.wsum[lane] = s;
-    }
-    __syncthreads();
-    const uint32_t excl = v - count + (warp ? S.wsum[warp - 1] : 0u);
-
-    // --- place this window's nibbles in output order ---
-    const unsigned long long s0 = start + excl;
-    if (count && s0 < end) {
-        const int n = (int)min((unsigned long long)count, end - s0);
-        const int dpos = (int)(s0 - base);
-        const int w0 = dpos >> 3, w1 = (dpos + n - 1) >> 3;
-        const int sh = (dpos & 7) * 4;
-        const int eoff = (dpos + n) & 7;
-        uint32_t prev = 0;
-        for (int j = w0, q = 0; j <= w1; ++j, ++q) {
-            const uint32_t cur = q < kSlotWords ? slot[q] : 0u;
-            uint32_t val = __funnelshift_r(cur, prev, sh);
-            prev = cur;
-            if (j == w1 && eoff) val &= 0xffffffffu << (32 - 4 * eoff);
-            if (j == w0 || j == w1)
-                atomicOr(&S.obuf[j], val);
-            else
-                S.obuf[j] = val;
-        }
-    }
-    __syncthreads();
-
-    // --- merge with sign+mantissa nibbles, 16 elements per store ---
-    for (int c = t; c < n_chunks; c += kThreads) {
-        const unsigned long long e0 = base + 16ull * c;
-        if (d.vec_ok && e0 >= start && e0 + 16 <= end) {
-            const uint2 ew = *reinterpret_cast<const uint2*>(&S.obuf[2 * c]);
-            const uint2 pw = __ldg(reinterpret_cast<const uint2*>(d.packed + (e0 >> 1)));
-            uint4 o;
-            merge8(ew.x, pw.x, o.x, o.y);
-            merge8(ew.y, pw.y, o.z, o.w);
-            *reinterpret_cast<uint4*>(d.out + e0) = o;
-        } else {
-            const unsigned long long a = e0 < start ? start : e0;
-            const unsigned long long b = e0 + 16 < end ? e0 + 16 : end;
-            for (unsigned long long i = a; i < b; ++i) d.out[i] = merge1(S, d, base, i);
-        }
-    }
-    __syncthreads();
+__device__ __forceinline__ int find_stream(const DevStream* s, int from, long long w) {
+    while (w >= s[from].group_begin + s[from].n_groups) ++from;
+    return from;
 }
 
 template <int MAXS>
 __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_constant__ Batch<MAXS> B) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem& S = *reinterpret_cast<Smem*>(smem_raw);
+    const int t = threadIdx.x;
     const long long total = B.total_groups;
     const long long lo = (long long)blockIdx.x * total / gridDim.x;
     const long long hi = (long long)(blockIdx.x + 1) * total / gridDim.x;
-    int si = -1;
+    if (lo >= hi) return;
+
+    int si = find_stream(B.s, 0, lo);
+    stage_window_bytes(S, 0, B.s[si], lo - B.s[si].group_begin);
+    cp_async_commit();
+    GroupRange r = group_range(B.s[si], lo - B.s[si].group_begin);
+    build_tables(S, B.s[si]);
+
     for (long long w = lo; w < hi; ++w) {
-        int ns = si < 0 ? 0 : si;
-        while (w >= B.s[ns].group_begin + B.s[ns].n_groups) ++ns;
-        if (ns != si) {
-            si = ns;
-            build_tables(S, B.s[si]);
-            __syncthreads();
+        const int buf = (int)((w - lo) & 1);
+        const DevStream& d = B.s[si];
+        const long long g = w - d.group_begin;
+        const unsigned long long start = r.start, end = r.end;
+        const unsigned long long base = start & ~15ull;
+        const int n_chunks = (int)((end - base + 15) >> 4);
+
+        // Stage this group's packed nibbles, the next group's window bytes,
+        // and fetch the next group's output range.
+        const long long p0 = (long long)(base >> 1) & ~15ll;
+        const int psize = (int)((((long long)((base >> 1) + 8 * (unsigned long long)n_chunks) - p0) + 15) & ~15ll);
+        stage(S.pack, d.packed, p0, psize, d.n_elements >> 1, d.async_ok);
+        cp_async_commit();
+        int sn = si;
+        if (w + 1 < hi) {
+            sn = find_stream(B.s, si, w + 1);
+            const long long gn = w + 1 - B.s[sn].group_begin;
+            stage_window_bytes(S, buf ^ 1, B.s[sn], gn);
+            r = group_range(B.s[sn], gn);
         }
-        decode_group(S, B.s[si], w - B.s[si].group_begin);
+        cp_async_commit();
+
+        for (int i = t; i < 2 * n_chunks; i += kThreads) S.obuf[i] = 0;
+        cp_async_wait<2>();  // this group's window bytes
+        __syncthreads();
+
+        // --- decode this thread's window ---
+        uint32_t* slot = S.slot + t * kSlotWords;
+        uint32_t count = 0;
+        if ((g * kThreads + t) * (long long)kWindowBytes < d.n_bytes) {
+            const uint2 raw = *reinterpret_cast<const uint2*>(S.enc[buf] + t * kWindowBytes);
+            const uint32_t r16 = *reinterpret_cast<const unsigned short*>(S.enc[buf] + t * kWindowBytes + 8);
+            const uint32_t gb = S.gaps[buf][t >> 1];
+            count = decode_window(S, slot, __byte_perm(raw.x, 0, 0x0123), __byte_perm(raw.y, 0, 0x0123),
+                                  ((r16 & 0xffu) << 8) | (r16 >> 8), (t & 1) ? (gb & 15u) : (gb >> 4));
+        }
+        // Windows wholly past n_bytes only follow the last real code: they place nothing.
+
+        // --- block exclusive scan of window counts (decode.cu:114-148) ---
+        const int lane = t & 31, warp = t >> 5;
+        uint32_t v = count;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += y;
+        }
+        if (lane == 31) S.wsum[warp] = v;
+        __syncthreads();
+        if (warp == 0) {
+            uint32_t s = lane < kThreads / 32 ? S.wsum[lane] : 0u;
+#pragma unroll
+            for (int o = 1; o < kThreads / 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(0xffffffffu, s, o);
+                if (lane >= o) s += y;
+            }
+            if (lane < kThreads / 32) S.wsum[lane] = s;
+        }
+        __syncthreads();
+        const uint32_t excl = v - count + (warp ? S.wsum[warp - 1] : 0u);
+
+        // --- place this window's nibbles in output order ---
+        const unsigned long long s0 = start + excl;
+        if (count && s0 < end) {
+            const uint32_t n = (uint32_t)min((unsigned long long)count, end - s0);
+            const uint32_t dpos = (uint32_t)(s0 - base);
+            const uint32_t w0 = dpos >> 3, nw = ((dpos + n - 1) >> 3) - w0;  // words after the first
+            const uint32_t sh = (dpos & 7) * 4;
+            const uint32_t tail = (dpos + n) & 7 ? 0xffffffffu << (32 - 4 * ((dpos + n) & 7)) : 0xffffffffu;
+            uint32_t prev = slot[0];
+            uint32_t first = __funnelshift_r(prev, 0u, sh);
+            if (nw == 0) first &= tail;
+            atomicOr(&S.obuf[w0], first);
+            for (uint32_t q = 1; q < nw; ++q) {
+                const uint32_t cur = slot[q];
+                S.obuf[w0 + q] = __funnelshift_r(cur, prev, sh);
+                prev = cur;
+            }
+            if (nw) {
+                const uint32_t cur = nw < kSlotWords ? slot[nw] : 0u;
+                atomicOr(&S.obuf[w0 + nw], __funnelshift_r(cur, prev, sh) & tail);
+            }
+        }
+        cp_async_wait<1>();  // this group's packed nibbles
+        __syncthreads();
+
+        // --- merge with sign+mantissa nibbles, 16 elements per store ---
+        const uint8_t* pk = S.pack + ((base >> 1) - p0);
+        for (int c = t; c < n_chunks; c += kThreads) {
+            const unsigned long long e0 = base + 16ull * c;
+            const uint2 ew = *reinterpret_cast<const uint2*>(&S.obuf[2 * c]);
+            const uint2 pw = *reinterpret_cast<const uint2*>(pk + 8 * c);
+            uint4 o;
+            merge8(ew.x, pw.x, o.x, o.y);
+            merge8(ew.y, pw.y, o.z, o.w);
+            if (d.out16 && e0 >= start && e0 + 16 <= end) {
+                *reinterpret_cast<uint4*>(d.out + e0) = o;
+            } else {
+                const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+#pragma unroll
+                for (int k = 0; k < 16; ++k)
+                    if (e0 + k >= start && e0 + k < end) d.out[e0 + k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
+            }
+        }
+        __syncthreads();
+
+        if (sn != si) {  // next group belongs to another stream
+            si = sn;
+            build_tables(S, B.s[si]);
+        }
     }
+    cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------------------
@@ -461,9 +531,9 @@ int make_stream(const ecf8_stream& s, DevStream* d) {
     d->n_luts = s.n_luts;
     // A stream with no elements has nothing to place.
     d->n_groups = s.n_elements > 0 ? (int)groups : 0;
-    d->vec_ok = aligned(s.encoded, 8) && aligned(s.packed_other_4bits, 8) && aligned(s.outputs, 16);
+    d->async_ok = aligned(s.encoded, 16) && aligned(s.packed_other_4bits, 16) && aligned(s.gaps, 16);
+    d->out16 = aligned(s.outputs, 16);
     d->group_begin = 0;
-    d->pad_ = 0;
     return ECF8_OK;
 }
 
