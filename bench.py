@@ -98,7 +98,7 @@ class ClockSampler:
         0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
     }
 
-    def __init__(self, index, period=0.01):
+    def __init__(self, index, period=0.002):
         self.samples, self.reasons, self.max_mhz = [], 0, None
         self.period, self.ok = period, False
         try:
@@ -113,16 +113,21 @@ class ClockSampler:
 
     def _run(self):
         nv = self.nv
+        del nv
         while not self.stop:
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                self.reasons |= nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-            except Exception:
-                pass
+            self.sample()
             time.sleep(self.period)
+
+    def sample(self):
+        try:
+            self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+            self.reasons |= self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except Exception:
+            pass
 
     def __enter__(self):
         if self.ok:
+            self.sample()
             self.stop = False
             self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
@@ -132,6 +137,7 @@ class ClockSampler:
         if self.ok:
             self.stop = True
             self.t.join()
+            self.sample()
 
     def summary(self):
         if not self.ok or not self.samples:
