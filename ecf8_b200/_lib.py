@@ -15,6 +15,8 @@ OK = 0
 ERR_INVALID_ARGUMENT = 1
 ERR_UNSUPPORTED = 2
 ERR_CUDA = 3
+ERR_TOO_LARGE = 4
+NOALLOC_MAX_ELEMENTS = 268435456
 
 MAX_LUTS = 18
 MAX_BATCH = 128
@@ -56,6 +58,9 @@ SIGNATURES = {
     "ecf8_encode_emit": (ctypes.c_int, [_c_u8p, _i64, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32),
                                         ctypes.c_int, ctypes.c_uint32, ctypes.c_void_p, _c_u8p, _i64, _i64,
                                         _c_u8p, _i64, ctypes.c_void_p, _i64, ctypes.c_void_p]),
+    "ecf8_encode_noalloc": (ctypes.c_int, [_c_u8p, _i64, ctypes.c_char_p, ctypes.POINTER(ctypes.c_uint32),
+                                           ctypes.c_int, ctypes.c_uint32, _c_u8p, _i64, _c_u8p, _i64,
+                                           ctypes.c_void_p, _i64, ctypes.c_void_p, ctypes.c_void_p]),
     "ecf8_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "ecf8_last_cuda_error": (ctypes.c_int, []),
     "ecf8_abi_version": (ctypes.c_int, []),

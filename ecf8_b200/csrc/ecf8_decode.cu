@@ -624,6 +624,8 @@ const char* ecf8_status_string(int status) {
         case ECF8_ERR_INVALID_ARGUMENT: return "invalid argument";
         case ECF8_ERR_UNSUPPORTED: return "unsupported stream format parameters";
         case ECF8_ERR_CUDA: return "CUDA runtime error";
+        case ECF8_ERR_TOO_LARGE:
+            return "stream longer than the no-allocation packer's built-in scratch (268,435,456 elements)";
         default: return "unknown status";
     }
 }

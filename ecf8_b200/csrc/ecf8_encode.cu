@@ -23,6 +23,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "ecf8.h"
 
 namespace ecf8enc {
@@ -292,6 +294,29 @@ int make_table(const uint8_t* code_bits, const uint32_t* code_values, int eof_bi
     return ECF8_OK;
 }
 
+// --- No-allocation variant --------------------------------------------------
+// Chunk bit offsets (+ total) and the 3-entry plan for streams of up to
+// kStaticMaxChunks chunks live in this file-scope array instead of a
+// caller-provided workspace.  One copy per GPU that loads the library,
+// held until the process exits.
+constexpr long long kStaticMaxChunks = 65536;  // 65536 x 4096 = 268,435,456 elements
+static_assert((long long)ECF8_NOALLOC_MAX_ELEMENTS == kStaticMaxChunks * kChunk, "limit mismatch");
+__device__ __align__(256) unsigned long long g_static_scratch[kStaticMaxChunks + 1 + 3];
+
+constexpr int kMaxDevices = 64;
+std::once_flag g_scratch_once[kMaxDevices];
+void* g_scratch_ptr[kMaxDevices];
+int g_scratch_status[kMaxDevices];
+
+// Writes the trailing output position from the plan the same launch sequence computed.
+__global__ void op_tail_from_plan_kernel(uint64_t* op, const unsigned long long* plan, long long n) {
+    op[plan[2] - 1] = (uint64_t)n;
+}
+
+__global__ void copy_plan_kernel(uint64_t* sizes, const unsigned long long* plan) {
+    if (threadIdx.x < 3) sizes[threadIdx.x] = plan[threadIdx.x];
+}
+
 }  // namespace
 }  // namespace ecf8enc
 
@@ -354,6 +379,71 @@ int ecf8_encode_emit(const uint8_t* exponents, int64_t n, const uint8_t* code_bi
         emit_kernel<<<(unsigned)chunks, kThreads, 0, s>>>(exponents, n, T, chunk, encoded, n_bytes,
                                                           reinterpret_cast<uint32_t*>(gaps), output_positions);
     op_tail_kernel<<<1, 1, 0, s>>>(output_positions, n_output_positions, n);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e);
+    return ECF8_OK;
+}
+
+// Single-call packer for callers that cannot allocate device memory; see
+// include/ecf8.h.  Its scratch is the file-scope array g_static_scratch.
+int ecf8_encode_noalloc(const uint8_t* exponents, int64_t n, const uint8_t* code_bits,
+                        const uint32_t* code_values, int eof_bits, uint32_t eof_value, uint8_t* encoded,
+                        int64_t encoded_capacity, uint8_t* gaps, int64_t gaps_capacity,
+                        uint64_t* output_positions, int64_t output_positions_capacity, uint64_t* sizes,
+                        void* cuda_stream) {
+    using namespace ecf8enc;
+    CodeTable T;
+    int st = make_table(code_bits, code_values, eof_bits, eof_value, &T);
+    if (st != ECF8_OK) return st;
+    if (!code_values || n < 0 || (n > 0 && !exponents) || !sizes || !output_positions)
+        return ECF8_ERR_INVALID_ARGUMENT;
+    if (n > (int64_t)ECF8_NOALLOC_MAX_ELEMENTS) return ECF8_ERR_TOO_LARGE;
+    // Capacities must cover the longest stream this code table can give for n
+    // symbols (every symbol at the longest code length).
+    int max_bits = 0;
+    for (int k = 0; k < 16; ++k) max_bits = code_bits[k] > max_bits ? code_bits[k] : max_bits;
+    const long long group_bytes = (long long)ECF8_THREADS_PER_BLOCK * ECF8_BYTES_PER_THREAD;
+    const long long max_stream_bits = (long long)n * max_bits;
+    const long long max_bytes = (max_stream_bits + 7) / 8;
+    const long long max_groups = (max_bytes + group_bytes - 1) / group_bytes;
+    if (encoded_capacity < ((max_bytes + 3) & ~3LL) || gaps_capacity < max_groups * (ECF8_THREADS_PER_BLOCK / 2) ||
+        output_positions_capacity < max_groups + 2)
+        return ECF8_ERR_INVALID_ARGUMENT;
+    if ((max_bytes > 0 && (!encoded || !gaps)) || (reinterpret_cast<uintptr_t>(encoded) & 3) ||
+        (reinterpret_cast<uintptr_t>(gaps) & 3) || (reinterpret_cast<uintptr_t>(output_positions) & 7) ||
+        (reinterpret_cast<uintptr_t>(sizes) & 7))
+        return ECF8_ERR_INVALID_ARGUMENT;
+    // Set-up once per device, with that device current: the device address of
+    // the scratch array (its name in host code is not a device pointer).
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (dev < 0 || dev >= kMaxDevices) return ECF8_ERR_UNSUPPORTED;
+    std::call_once(g_scratch_once[dev], [dev]() {
+        void* ptr = nullptr;
+        cudaError_t err = cudaGetSymbolAddress(&ptr, g_static_scratch);
+        g_scratch_status[dev] = (int)err;
+        g_scratch_ptr[dev] = ptr;
+    });
+    if (g_scratch_status[dev] != cudaSuccess) return cuda_fail((cudaError_t)g_scratch_status[dev]);
+    unsigned long long* chunk = static_cast<unsigned long long*>(g_scratch_ptr[dev]);
+    const long long chunks = (n + kChunk - 1) / kChunk;
+    unsigned long long* plan = chunk + chunks + 1;
+    cudaStream_t s = (cudaStream_t)cuda_stream;
+    // The scratch keeps the previous call's values; every entry this call
+    // reads (chunk sums, their scan, the plan) is rewritten below before it is
+    // read.  The outputs are cleared in full.
+    if (encoded_capacity > 0) e = cudaMemsetAsync(encoded, 0, (size_t)encoded_capacity, s);
+    if (e == cudaSuccess && gaps_capacity > 0) e = cudaMemsetAsync(gaps, 0, (size_t)gaps_capacity, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(output_positions, 0, (size_t)output_positions_capacity * 8, s);
+    if (e != cudaSuccess) return cuda_fail(e);
+    if (chunks > 0) chunk_bits_kernel<<<(unsigned)chunks, kThreads, 0, s>>>(exponents, n, T, chunk);
+    scan_plan_kernel<<<1, kScanThreads, 0, s>>>(exponents, n, T, chunk, chunks, plan);
+    if (chunks > 0)
+        emit_kernel<<<(unsigned)chunks, kThreads, 0, s>>>(exponents, n, T, chunk, encoded, 0,
+                                                          reinterpret_cast<uint32_t*>(gaps), output_positions);
+    op_tail_from_plan_kernel<<<1, 1, 0, s>>>(output_positions, plan, n);
+    copy_plan_kernel<<<1, 32, 0, s>>>(sizes, plan);
     e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
     return ECF8_OK;

@@ -39,6 +39,7 @@ extern "C" {
 #define ECF8_ERR_INVALID_ARGUMENT 1 /* a size or pointer is inconsistent */
 #define ECF8_ERR_UNSUPPORTED 2      /* threads_per_block / bytes_per_thread */
 #define ECF8_ERR_CUDA 3             /* a CUDA runtime call failed */
+#define ECF8_ERR_TOO_LARGE 4        /* above ECF8_NOALLOC_MAX_ELEMENTS */
 
 /* Limits of the stream format the kernels accept. */
 #define ECF8_BYTES_PER_THREAD 8    /* window size in bytes (decode.cu:5) */
@@ -125,6 +126,43 @@ int ecf8_encode_emit(const uint8_t* exponents, int64_t n,
                      uint8_t* gaps, int64_t n_gap_bytes,
                      uint64_t* output_positions, int64_t n_output_positions,
                      void* cuda_stream);
+
+/*
+ * ecf8_encode_noalloc: the packer above in one call that allocates nothing.
+ * It has no counterpart in the reference (whose packer runs in Python on the
+ * host).  It is for callers that cannot hand the library extra device memory:
+ * code running inside another framework that owns all device memory through
+ * its own pool (a stray cudaMalloc can fail there, or fragment the pool), and
+ * latency-sensitive loaders for which cudaMalloc's implicit device
+ * synchronisation would stall other streams.  Such a caller passes only the
+ * exponents, the code table and output buffers.
+ *
+ * Its working memory (per-chunk bit offsets) is a fixed array inside the
+ * library, one per GPU that loads it, kept until the process exits, sized
+ * for n <= ECF8_NOALLOC_MAX_ELEMENTS exponents (about 0.5 MB); larger n
+ * returns ECF8_ERR_TOO_LARGE.  The first call on a device looks up that
+ * array's device address; make the first call on each device before any
+ * stream capture.  All calls share the array: calls whose work overlaps on
+ * the GPU (different streams, or different host threads) race and must be
+ * serialised by the caller.
+ *
+ * Outputs are cleared in full and must hold the longest stream the code
+ * table allows for n symbols (L = the longest code length in code_bits):
+ * encoded_capacity >= ceil(n*L/8) rounded up to 4, gaps_capacity >=
+ * ceil(ceil(n*L/8)/4096)*256 bytes, output_positions_capacity >= that group
+ * count + 2 entries.  sizes (3 u64, device) receives the total bit count, the
+ * encoded byte count and the number of output_positions entries; the buffers
+ * equal ecf8_encode_emit()'s for the same input up to those sizes (gaps up to
+ * ceil(n_bytes/4096)*256 bytes).  Asynchronous on cuda_stream.
+ */
+#define ECF8_NOALLOC_MAX_ELEMENTS 268435456LL
+int ecf8_encode_noalloc(const uint8_t* exponents, int64_t n,
+                        const uint8_t* code_bits, const uint32_t* code_values,
+                        int eof_bits, uint32_t eof_value, uint8_t* encoded,
+                        int64_t encoded_capacity, uint8_t* gaps,
+                        int64_t gaps_capacity, uint64_t* output_positions,
+                        int64_t output_positions_capacity, uint64_t* sizes,
+                        void* cuda_stream);
 
 /* Human-readable text for a status code. */
 const char* ecf8_status_string(int status);
