@@ -18,8 +18,10 @@ from .codec import (  # noqa: F401
 from .run import (  # noqa: F401
     DFloatDiffSynthModelFP8,
     DFloatModel,
+    HostStreamDecoder,
     TensorManager,
     _decode,
+    build_decode_table,
     decode_stream,
     decode_streams,
     get_dfloat_model_name_or_path,

@@ -43,6 +43,7 @@ class Ecf8Stream(ctypes.Structure):
         ("n_gap_bytes", ctypes.c_int64),
         ("outputs", ctypes.c_void_p),
         ("n_elements", ctypes.c_int64),
+        ("table", ctypes.c_void_p),
     ]
 
 
@@ -50,6 +51,7 @@ class Ecf8Stream(ctypes.Structure):
 SIGNATURES = {
     "ecf8_decode": (ctypes.c_int, [_c_u8p, _c_u8p, _c_u8p, _c_u8p, _c_u8p, _c_u8p, ctypes.c_int,
                                    _i64, _i64, _i64, _i64, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]),
+    "ecf8_build_table": (ctypes.c_int, [_c_u8p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     "ecf8_decode_batch": (ctypes.c_int, [ctypes.POINTER(Ecf8Stream), ctypes.c_int, ctypes.c_int,
                                          ctypes.c_int, ctypes.c_void_p]),
     "ecf8_encode_workspace_bytes": (ctypes.c_int64, [_i64]),
@@ -91,7 +93,7 @@ def lib():
                 fn = getattr(handle, name)
                 fn.restype = res
                 fn.argtypes = args
-            if handle.ecf8_abi_version() != 1:
+            if handle.ecf8_abi_version() != 2:
                 raise RuntimeError("ECF8 CUDA library ABI version mismatch")
             _lib = handle
     return _lib

@@ -5,25 +5,26 @@
 // like the reference kernel dfloat/run/decode.cu:16-211, with a different
 // design:
 //
-//  * Persistent CTAs.  Each CTA of 512 threads walks a contiguous range of
+//  * Persistent CTAs.  Each CTA of 256 threads walks a contiguous range of
 //    4096-byte groups (one reference thread block's worth of stream), across
-//    one or many streams of a batch, so per-stream set-up is paid once per
-//    CTA, not once per group.
-//  * Multi-symbol table.  From the reference's two-level byte LUTs each CTA
-//    derives, in shared memory, a 4096-entry table indexed by the next 12
-//    stream bits that yields up to five whole symbols, the bits they use and
-//    their start offsets.  A window of 64 bits (about 25 symbols for trained
-//    weights) costs ~6 dependent lookups instead of ~25 chains of 2-3.
-//  * Single decode pass.  The reference decodes every window twice (count,
-//    then write).  Here each thread decodes its window once into a private
-//    shared-memory slot of nibbles, a warp-shuffle + block scan places every
-//    window, and the slots are funnel-shifted into an output-ordered nibble
-//    buffer.
-//  * Coalesced merge.  The exponent nibbles and the packed sign+mantissa
+//    one or many streams of a batch.
+//  * Multi-symbol table.  A 4096-entry table indexed by the next 12 stream
+//    bits yields up to five whole symbols, the bits they use and their count.
+//    It is a pure function of the stream's LUTs: ecf8_build_table() derives
+//    it once per stream (at load time) and every CTA copies it into shared
+//    memory; without a prepared table each CTA derives it itself.
+//  * Two windows per thread, one decode pass.  Each thread decodes its two
+//    adjacent 64-bit windows as one continuous run (the first window's gap
+//    gives the start) into a private shared-memory slot of nibbles; a
+//    warp-shuffle scan places each run; slots are funnel-shifted into an
+//    output-ordered nibble buffer.
+//  * Staging and merge.  Each group's bitstream and gaps are staged into
+//    shared memory with 16-byte cp.async one group ahead, its packed
+//    sign+mantissa nibbles at the start of the group; exponent and packed
 //    nibbles are merged 16 elements at a time with byte-permute/logic ops and
-//    written with one 16-byte store per thread, instead of one byte per thread.
+//    written with one 16-byte store.
 //
-// No inter-CTA communication, no global scratch, no allocation.
+// No inter-CTA communication, no global scratch, no allocation, no spin-waits.
 
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -36,36 +37,38 @@
 namespace ecf8 {
 namespace {
 
-constexpr int kThreads = ECF8_THREADS_PER_BLOCK;        // windows per group
-constexpr int kWindowBytes = ECF8_BYTES_PER_THREAD;     // bytes per window
-constexpr int kGroupBytes = kThreads * kWindowBytes;    // 4096
+constexpr int kGroupWindows = ECF8_THREADS_PER_BLOCK;   // windows per group (512)
+constexpr int kWindowBytes = ECF8_BYTES_PER_THREAD;     // bytes per window (8)
+constexpr int kThreads = kGroupWindows / 2;             // CTA size: two windows per thread
+constexpr int kGroupBytes = kGroupWindows * kWindowBytes;  // 4096
 constexpr int kTabBits = 12;                            // multi-symbol table width
 constexpr int kTabSize = 1 << kTabBits;
 constexpr int kMaxSymsPerEntry = 5;                     // 5 nibbles fit in bits 31..12
-constexpr int kSlotWords = 9;                           // 72 nibbles >= 64 + 4 overshoot
-constexpr int kMaxGroupElems = kThreads * 64;           // one symbol per bit at most
+constexpr int kSlotWords = 17;                          // 136 nibbles >= 128 + 4 overshoot (odd stride)
+constexpr int kMaxGroupElems = kGroupWindows * 64;      // one symbol per bit at most
 constexpr int kObufWords = (kMaxGroupElems + 32) / 8;   // + 15 head pad, round to 16
 constexpr int kLutRows = ECF8_MAX_LUTS - 1;             // decode rows (row 0 + prefixes)
 constexpr int kEncStage = kGroupBytes + 16;             // group bytes + look-ahead, 16-byte units
-constexpr int kGapStage = kThreads / 2;                 // 4 bits per window
-constexpr int kPackStage = kMaxGroupElems / 2 + 32;     // packed nibbles of one group (+ alignment)
+constexpr int kGapStage = kGroupWindows / 2;            // 4 bits per window
+constexpr int kPackChunks = 1024;                       // 16-element chunks whose nibbles are staged
+constexpr int kPackStage = kPackChunks * 8 + 16;        // the rest of a (rare) longer group: global loads
 
 struct alignas(16) Smem {
     uint32_t tab[kTabSize];                  // multi-symbol entries
-    uint32_t slot[kThreads * kSlotWords];    // per-window decoded nibbles (MSB first)
+    uint32_t slot[kThreads * kSlotWords];    // per-thread decoded nibbles (MSB first)
     uint32_t obuf[kObufWords];               // output-ordered exponent nibbles
     uint8_t enc[2][kEncStage];               // staged bitstream, double buffered
     uint8_t gaps[2][kGapStage];              // staged gaps, double buffered
     uint8_t pack[kPackStage];                // staged sign+mantissa nibbles
-    uint16_t tmask[kTabSize + 8];            // start offsets of an entry's symbols (+ sentinel)
     uint8_t lut[kLutRows * 256];             // reference LUT rows 0..n_luts-2, zero padded
     uint8_t lens[256];                       // reference LUT last row: code lengths
     uint32_t chg[kLutRows * 8];              // per row: bit b set if entry b != entry b-1
-    uint32_t wsum[kThreads / 32];            // block-scan warp totals
+    uint32_t wsum[kThreads / 32];            // scan: warp totals
 };
 static_assert(offsetof(Smem, obuf) % 16 == 0, "obuf must allow 8-byte vector reads");
 static_assert(offsetof(Smem, enc) % 16 == 0 && kEncStage % 16 == 0, "cp.async targets are 16-byte units");
 static_assert(offsetof(Smem, gaps) % 16 == 0 && offsetof(Smem, pack) % 16 == 0, "cp.async alignment");
+static_assert(offsetof(Smem, slot) % 16 == 0 && offsetof(Smem, tab) % 16 == 0, "vector copies");
 
 struct DevStream {
     const uint8_t* luts;
@@ -74,6 +77,7 @@ struct DevStream {
     const uint64_t* op;
     const uint8_t* gaps;
     uint8_t* out;
+    const uint32_t* table;  // prepared multi-symbol table (4096 entries) or null
     long long n_bytes;
     long long n_elements;
     long long n_op;
@@ -122,12 +126,12 @@ __device__ __forceinline__ void stage(uint8_t* dst, const uint8_t* src, long lon
 }
 
 // ---------------------------------------------------------------------------
-// Per-stream set-up: copy the reference LUTs and derive the multi-symbol table.
-// Entry layout (u32): bits 31..12 up to five 4-bit symbols, first symbol in
-// the top nibble; bits 11..8 the number of stream bits the symbols use; bits
-// 4..0 four times the symbol count (so the entry is directly a funnel-shift
-// amount).  An all-zero entry means no complete code starts the pattern
-// within 12 bits; the decoder then uses the two-level LUT directly.
+// Per-stream set-up.  Entry layout (u32): bits 31..12 up to five 4-bit
+// symbols, first symbol in the top nibble; bits 11..8 the number of stream
+// bits the symbols use; bits 4..0 four times the symbol count (so the entry
+// is directly a funnel-shift amount).  An all-zero entry means no complete
+// code starts the pattern within 12 bits; the decoder then uses the
+// two-level LUT directly.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t lut_symbol(const Smem& S, uint32_t top) {
     // `top` holds the next >= 16 stream bits left-aligned (dfloat/run/decode.cu:86-88).
@@ -141,6 +145,17 @@ __device__ __forceinline__ uint32_t code_length(const Smem& S, uint32_t sym) {
     // code (the reference would spin there); it advances by one bit.
     uint32_t len = S.lens[sym & 255u];
     return len ? len : 1u;
+}
+
+// Bit j set for the end offset of each symbol of entry e (offsets 1..12).
+__device__ __forceinline__ uint32_t entry_ends(const Smem& S, uint32_t e) {
+    const uint32_t c = (e & 31u) >> 2;
+    uint32_t pos = 0, mask = 0;
+    for (uint32_t i = 0; i < c; ++i) {
+        pos += code_length(S, (e >> (28 - 4 * i)) & 15u);
+        mask |= 1u << pos;
+    }
+    return mask;
 }
 
 // True when LUT row `row` holds one value over the 2^pad entries starting at
@@ -183,15 +198,20 @@ __device__ __forceinline__ bool real_code(const Smem& S, uint32_t v, uint32_t& s
     return true;
 }
 
-__device__ void build_tables(Smem& S, const DevStream& d) {
+// Copies the stream's LUT rows into shared memory (all threads; ends with a barrier).
+__device__ void load_luts(Smem& S, const DevStream& d) {
     const int t = threadIdx.x;
     for (int i = t; i < kLutRows * 256; i += kThreads) {
         const int row = i >> 8;
         S.lut[i] = (row < d.n_luts - 1) ? __ldg(d.luts + i) : (uint8_t)0;
     }
     for (int i = t; i < 256; i += kThreads) S.lens[i] = __ldg(d.luts + (d.n_luts - 1) * 256 + i);
-    if (t < 8) S.tmask[kTabSize + t] = 1;  // start mask of a single directly decoded code
     __syncthreads();
+}
+
+// Derives the multi-symbol table from the LUTs in shared memory (all threads).
+__device__ void derive_table(Smem& S) {
+    const int t = threadIdx.x;
     // Change bitmaps, one ballot per 32 entries (rows are 256 = 8 x 32 wide).
     for (int i = t; i < kLutRows * 256; i += kThreads) {
         const bool change = (i & 255) && S.lut[i] != S.lut[i - 1];
@@ -201,15 +221,13 @@ __device__ void build_tables(Smem& S, const DevStream& d) {
     __syncthreads();
     // Entry 0 (all-zero pattern) greedily.
     if (t == 0) {
-        uint32_t syms = 0, mask = 0, pos = 0, c = 0, sym, len;
+        uint32_t syms = 0, pos = 0, c = 0, sym, len;
         while (c < (uint32_t)kMaxSymsPerEntry && real_code(S, 0, sym, len) && pos + len <= (uint32_t)kTabBits) {
             syms |= (sym & 15u) << (28 - 4 * c);
-            mask |= 1u << pos;
             pos += len;
             ++c;
         }
         S.tab[0] = syms | (pos << 8) | (4 * c);
-        S.tmask[0] = (uint16_t)mask;
     }
     __syncthreads();
     // Entry x from entry y = (x << l) & 0xfff, where l is x's first code length:
@@ -220,54 +238,63 @@ __device__ void build_tables(Smem& S, const DevStream& d) {
         const int n = 1 << (kTabBits - 1 - tz);
         for (int j = t; j < n; j += kThreads) {
             const uint32_t x = (uint32_t)(2 * j + 1) << tz;
-            uint32_t sym, len, ent = 0, msk = 0;
+            uint32_t sym, len, ent = 0;
             if (real_code(S, x << 4, sym, len) && len <= (uint32_t)kTabBits) {
-                uint32_t kept = 0, endk = 0, rest = 0, mrest = 0;
+                uint32_t kept = 0, endk = 0, rest = 0;
                 if (len < (uint32_t)kTabBits) {
-                    const uint32_t y = (x << len) & (kTabSize - 1);
-                    const uint32_t ey = S.tab[y], my = S.tmask[y];
-                    const uint32_t endmask = (ey & 31u) ? ((my & ~1u) | (1u << ((ey >> 8) & 15u))) : 0u;
-                    kept = min(__popc(endmask & ((2u << (kTabBits - len)) - 1u)), kMaxSymsPerEntry - 1);
+                    const uint32_t ey = S.tab[(x << len) & (kTabSize - 1)];
+                    const uint32_t ends = entry_ends(S, ey);
+                    kept = min(__popc(ends & ((2u << (kTabBits - len)) - 1u)), kMaxSymsPerEntry - 1);
                     if (kept) {
-                        endk = __fns(endmask, 0, (int)kept);
+                        endk = __fns(ends, 0, (int)kept);
                         rest = (ey >> 4) & (((1u << (4 * kept)) - 1u) << (28 - 4 * kept));
-                        mrest = my & ((1u << endk) - 1u);
                     }
                 }
                 ent = ((sym & 15u) << 28) | rest | ((len + endk) << 8) | (4 * (1 + kept));
-                msk = 1u | (mrest << len);
             }
             S.tab[x] = ent;
-            S.tmask[x] = (uint16_t)msk;
         }
         __syncthreads();
     }
 }
 
+// LUTs plus the table: copied when prepared, derived otherwise (ends with a barrier).
+__device__ void setup_stream(Smem& S, const DevStream& d) {
+    if (d.table) {
+        const uint4* src = reinterpret_cast<const uint4*>(d.table);
+        uint4* dst = reinterpret_cast<uint4*>(S.tab);
+        for (int i = threadIdx.x; i < kTabSize / 4; i += kThreads) dst[i] = __ldg(src + i);
+        load_luts(S, d);
+    } else {
+        load_luts(S, d);
+        derive_table(S);
+    }
+}
+
 // ---------------------------------------------------------------------------
-// Window decode.  Stream bits [p, 80) of the window (64 bits + 16 look-ahead)
-// sit left-aligned in the 96-bit shift register (h:m:x).  Decoded nibbles go
+// Run decode.  A thread's run is its two adjacent windows: stream bits
+// [gap, 128) of the pair, with the 32 bits after the pair as look-ahead.  The
+// next 96 bits sit left-aligned in the shift register (h:m:x); p is the bit
+// offset of its top within the current 64-bit half.  Decoded nibbles go
 // through a 64-bit accumulator (ah:al) into the thread's shared-memory slot,
-// eight at a time.  Returns the number of codes that start in bits [gap, 64)
-// (decode.cu:65-112).
+// eight at a time.  Returns the number of codes that start in run bits
+// [gap, 128) -- the two windows' counts of decode.cu:65-112 together.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t decode_window(const Smem& S, uint32_t* slot, uint32_t w0, uint32_t w1,
-                                                  uint32_t la, uint32_t gap) {
+__device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t* slot, uint32_t w0, uint32_t w1,
+                                               uint32_t w2, uint32_t w3, uint32_t w4, uint32_t gap) {
     uint32_t h = __funnelshift_l(w1, w0, gap);
-    uint32_t m = __funnelshift_l(la << 16, w1, gap);
-    uint32_t x = (la << 16) << gap;
-    uint32_t p = gap, ah = 0, al = 0, m4 = 0;
+    uint32_t m = __funnelshift_l(w2, w1, gap);
+    uint32_t x = w2 << gap;
+    uint32_t p = gap, ah = 0, al = 0, m4 = 0, second = 0;
     uint32_t* sp = slot;
-    uint32_t idx, e, b;
-    do {
-        idx = h >> (32 - kTabBits);
-        e = S.tab[idx];
+    uint32_t e, b;
+    for (;;) {
+        e = S.tab[h >> (32 - kTabBits)];
         b = (e >> 8) & 15u;
         if (b == 0) {  // no complete code within the table width: two-level LUT
             const uint32_t sym = lut_symbol(S, h);
             b = code_length(S, sym);
             e = ((sym & 15u) << 28) | 4u;
-            idx = kTabSize;
         }
         ah = __funnelshift_l(al, ah, e);  // append e's symbols; shift = e & 31 = 4 x count
         al = __funnelshift_l(e, al, e);
@@ -280,14 +307,29 @@ __device__ __forceinline__ uint32_t decode_window(const Smem& S, uint32_t* slot,
         m = __funnelshift_l(x, m, b);
         x <<= b;
         p += b;
-    } while (p < 64);
+        if (p >= 64) {
+            if (second) break;
+            second = 1;  // continue in the second window: bits [64, 160) of the run
+            p -= 64;
+            h = __funnelshift_l(w3, w2, p);
+            m = __funnelshift_l(w4, w3, p);
+            x = w4 << p;
+        }
+    }
     if (m4) *sp = al << (32 - m4);
     uint32_t n = (uint32_t)(sp - slot) * 8 + (m4 >> 2);
-    // The last step may have taken codes that start at or after bit 64; they
-    // belong to the next window.
+    // The last step may have taken codes that start at or after the run's
+    // end; they belong to the next run.
     const uint32_t room = 64 - (p - b);
-    if (room < (uint32_t)kTabBits)
-        n -= ((e & 31u) >> 2) - __popc((uint32_t)S.tmask[idx] & ((1u << room) - 1u));
+    if (room < (uint32_t)kTabBits) {
+        const uint32_t c = (e & 31u) >> 2;
+        uint32_t start = 0, keep = 0;
+        for (uint32_t i = 0; i < c; ++i) {
+            keep += start < room;
+            start += code_length(S, (e >> (28 - 4 * i)) & 15u);
+        }
+        n -= c - keep;
+    }
     return n;
 }
 
@@ -327,11 +369,23 @@ __device__ __forceinline__ int find_stream(const DevStream* s, int from, long lo
     return from;
 }
 
+// Eight packed bytes of the stream at byte offset `off` (multiple of 8); bytes
+// at or past n_elements / 2 read as 0.
+__device__ __forceinline__ uint2 packed8(const DevStream& d, unsigned long long off) {
+    const unsigned long long limit = (unsigned long long)d.n_elements >> 1;
+    if (d.async_ok && off + 8 <= limit) return __ldg(reinterpret_cast<const uint2*>(d.packed + off));
+    uint32_t b[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) b[k] = off + k < limit ? __ldg(d.packed + off + k) : 0u;
+    return make_uint2(b[0] | b[1] << 8 | b[2] << 16 | b[3] << 24, b[4] | b[5] << 8 | b[6] << 16 | b[7] << 24);
+}
+
 template <int MAXS>
-__global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_constant__ Batch<MAXS> B) {
+__global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_constant__ Batch<MAXS> B) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem& S = *reinterpret_cast<Smem*>(smem_raw);
     const int t = threadIdx.x;
+    const int lane = t & 31, warp = t >> 5;
     const long long total = B.total_groups;
     const long long lo = (long long)blockIdx.x * total / gridDim.x;
     const long long hi = (long long)(blockIdx.x + 1) * total / gridDim.x;
@@ -341,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
     stage_window_bytes(S, 0, B.s[si], lo - B.s[si].group_begin);
     cp_async_commit();
     GroupRange r = group_range(B.s[si], lo - B.s[si].group_begin);
-    build_tables(S, B.s[si]);
+    setup_stream(S, B.s[si]);
 
     for (long long w = lo; w < hi; ++w) {
         const int buf = (int)((w - lo) & 1);
@@ -349,13 +403,18 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
         const long long g = w - d.group_begin;
         const unsigned long long start = r.start, end = r.end;
         const unsigned long long base = start & ~15ull;
-        const int n_chunks = (int)((end - base + 15) >> 4);
+        const uint32_t rs = (uint32_t)(start - base), re = (uint32_t)(end - base);  // range rel. to base
+        const int n_chunks = (int)((re + 15) >> 4);
 
-        // Stage this group's packed nibbles, the next group's window bytes,
-        // and fetch the next group's output range.
+        cp_async_wait<0>();  // this group's window bytes
+        __syncthreads();     // ... visible; previous group's merge done with pack / obuf / slots
+
+        // Stage this group's packed nibbles and the next group's window bytes;
+        // fetch the next group's output range.
         const long long p0 = (long long)(base >> 1) & ~15ll;
-        const int psize = (int)((((long long)((base >> 1) + 8 * (unsigned long long)n_chunks) - p0) + 15) & ~15ll);
-        stage(S.pack, d.packed, p0, psize, d.n_elements >> 1, d.async_ok);
+        const uint32_t pofs = (uint32_t)((base >> 1) - p0);  // 0 or 8
+        const int staged = n_chunks < kPackChunks ? n_chunks : kPackChunks;
+        stage(S.pack, d.packed, p0, (int)((pofs + 8 * staged + 15) & ~15u), d.n_elements >> 1, d.async_ok);
         cp_async_commit();
         int sn = si;
         if (w + 1 < hi) {
@@ -365,25 +424,21 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
             r = group_range(B.s[sn], gn);
         }
         cp_async_commit();
-
         for (int i = t; i < 2 * n_chunks; i += kThreads) S.obuf[i] = 0;
-        cp_async_wait<2>();  // this group's window bytes
-        __syncthreads();
 
-        // --- decode this thread's window ---
+        // --- decode this thread's window pair ---
         uint32_t* slot = S.slot + t * kSlotWords;
         uint32_t count = 0;
-        if ((g * kThreads + t) * (long long)kWindowBytes < d.n_bytes) {
-            const uint2 raw = *reinterpret_cast<const uint2*>(S.enc[buf] + t * kWindowBytes);
-            const uint32_t r16 = *reinterpret_cast<const unsigned short*>(S.enc[buf] + t * kWindowBytes + 8);
-            const uint32_t gb = S.gaps[buf][t >> 1];
-            count = decode_window(S, slot, __byte_perm(raw.x, 0, 0x0123), __byte_perm(raw.y, 0, 0x0123),
-                                  ((r16 & 0xffu) << 8) | (r16 >> 8), (t & 1) ? (gb & 15u) : (gb >> 4));
+        if (g * kGroupBytes + 16 * t < d.n_bytes) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(S.enc[buf] + 16 * t);
+            const uint32_t r4 = *reinterpret_cast<const uint32_t*>(S.enc[buf] + 16 * t + 16);
+            count = decode_run(S, slot, __byte_perm(raw.x, 0, 0x0123), __byte_perm(raw.y, 0, 0x0123),
+                               __byte_perm(raw.z, 0, 0x0123), __byte_perm(raw.w, 0, 0x0123),
+                               __byte_perm(r4, 0, 0x0123), S.gaps[buf][t] >> 4);
         }
-        // Windows wholly past n_bytes only follow the last real code: they place nothing.
+        // A pair wholly past n_bytes only follows the last real code: it places nothing.
 
-        // --- block exclusive scan of window counts (decode.cu:114-148) ---
-        const int lane = t & 31, warp = t >> 5;
+        // --- exclusive scan of run counts (decode.cu:114-148) ---
         uint32_t v = count;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -392,23 +447,19 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
         }
         if (lane == 31) S.wsum[warp] = v;
         __syncthreads();
-        if (warp == 0) {
-            uint32_t s = lane < kThreads / 32 ? S.wsum[lane] : 0u;
+        uint32_t ws = lane < kThreads / 32 ? S.wsum[lane] : 0u;
 #pragma unroll
-            for (int o = 1; o < kThreads / 32; o <<= 1) {
-                const uint32_t y = __shfl_up_sync(0xffffffffu, s, o);
-                if (lane >= o) s += y;
-            }
-            if (lane < kThreads / 32) S.wsum[lane] = s;
+        for (int o = 1; o < kThreads / 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(0xffffffffu, ws, o);
+            if (lane >= o) ws += y;
         }
-        __syncthreads();
-        const uint32_t excl = v - count + (warp ? S.wsum[warp - 1] : 0u);
+        const uint32_t wbase = __shfl_sync(0xffffffffu, ws, (warp + 31) & 31);
+        const uint32_t excl = v - count + (warp ? wbase : 0u);
 
-        // --- place this window's nibbles in output order ---
-        const unsigned long long s0 = start + excl;
-        if (count && s0 < end) {
-            const uint32_t n = (uint32_t)min((unsigned long long)count, end - s0);
-            const uint32_t dpos = (uint32_t)(s0 - base);
+        // --- place this run's nibbles in output order ---
+        const uint32_t dpos = rs + excl;
+        if (count && dpos < re) {
+            const uint32_t n = min(count, re - dpos);
             const uint32_t w0 = dpos >> 3, nw = ((dpos + n - 1) >> 3) - w0;  // words after the first
             const uint32_t sh = (dpos & 7) * 4;
             const uint32_t tail = (dpos + n) & 7 ? 0xffffffffu << (32 - 4 * ((dpos + n) & 7)) : 0xffffffffu;
@@ -430,31 +481,46 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const __grid_consta
         __syncthreads();
 
         // --- merge with sign+mantissa nibbles, 16 elements per store ---
-        const uint8_t* pk = S.pack + ((base >> 1) - p0);
+        const uint8_t* pk = S.pack + pofs;
         for (int c = t; c < n_chunks; c += kThreads) {
-            const unsigned long long e0 = base + 16ull * c;
+            const uint32_t e0 = 16u * c;
             const uint2 ew = *reinterpret_cast<const uint2*>(&S.obuf[2 * c]);
-            const uint2 pw = *reinterpret_cast<const uint2*>(pk + 8 * c);
+            const uint2 pw = c < kPackChunks ? *reinterpret_cast<const uint2*>(pk + 8 * c)
+                                             : packed8(d, (base >> 1) + 8ull * c);
             uint4 o;
             merge8(ew.x, pw.x, o.x, o.y);
             merge8(ew.y, pw.y, o.z, o.w);
-            if (d.out16 && e0 >= start && e0 + 16 <= end) {
-                *reinterpret_cast<uint4*>(d.out + e0) = o;
+            uint8_t* dst = d.out + base + e0;
+            if (d.out16 && e0 >= rs && e0 + 16 <= re) {
+                *reinterpret_cast<uint4*>(dst) = o;
             } else {
                 const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
 #pragma unroll
                 for (int k = 0; k < 16; ++k)
-                    if (e0 + k >= start && e0 + k < end) d.out[e0 + k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
+                    if (e0 + k >= rs && e0 + k < re) dst[k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
             }
         }
-        __syncthreads();
 
         if (sn != si) {  // next group belongs to another stream
             si = sn;
-            build_tables(S, B.s[si]);
+            __syncthreads();  // all decodes of this group are done with the tables
+            setup_stream(S, B.s[si]);
         }
     }
     cp_async_wait<0>();
+}
+
+// One CTA derives a stream's multi-symbol table and writes it to `table`.
+__global__ void __launch_bounds__(kThreads, 1) build_table_kernel(const uint8_t* luts, int n_luts,
+                                                                   uint32_t* table) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    Smem& S = *reinterpret_cast<Smem*>(smem_raw);
+    DevStream d{};
+    d.luts = luts;
+    d.n_luts = n_luts;
+    load_luts(S, d);
+    derive_table(S);
+    for (int i = threadIdx.x; i < kTabSize; i += kThreads) table[i] = S.tab[i];
 }
 
 // ---------------------------------------------------------------------------
@@ -492,6 +558,8 @@ int device_info(DeviceInfo* out) {
             err = cudaFuncSetAttribute(decode_kernel<ECF8_MAX_BATCH>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (err == cudaSuccess)
+            err = cudaFuncSetAttribute(build_table_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (err == cudaSuccess)
             err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&info.blocks_per_sm, decode_kernel<1>,
                                                                 kThreads, smem);
         g_device_status[dev] = (int)err;
@@ -510,11 +578,12 @@ int make_stream(const ecf8_stream& s, DevStream* d) {
     if (s.n_luts < 2 || s.n_luts > ECF8_MAX_LUTS) return ECF8_ERR_INVALID_ARGUMENT;
     if (s.n_bytes < 0 || s.n_elements < 0 || (s.n_elements & 1)) return ECF8_ERR_INVALID_ARGUMENT;
     if (s.n_output_positions < 1 || s.n_gap_bytes < 0) return ECF8_ERR_INVALID_ARGUMENT;
-    const long long group_bytes = (long long)kThreads * kWindowBytes;
+    const long long group_bytes = (long long)kGroupBytes;
     const long long groups = (s.n_bytes + group_bytes - 1) / group_bytes;
     if (groups > 0x7fffffffLL) return ECF8_ERR_INVALID_ARGUMENT;
     if (s.n_elements > 0 && s.n_bytes == 0) return ECF8_ERR_INVALID_ARGUMENT;
-    if (s.n_gap_bytes < groups * (kThreads / 2)) return ECF8_ERR_INVALID_ARGUMENT;
+    if (s.n_gap_bytes < groups * kGapStage) return ECF8_ERR_INVALID_ARGUMENT;
+    if (s.table && !aligned(s.table, 16)) return ECF8_ERR_INVALID_ARGUMENT;
     if (s.n_elements > 0 &&
         (!s.luts || !s.encoded || !s.packed_other_4bits || !s.output_positions || !s.gaps || !s.outputs))
         return ECF8_ERR_INVALID_ARGUMENT;
@@ -524,6 +593,7 @@ int make_stream(const ecf8_stream& s, DevStream* d) {
     d->packed = s.packed_other_4bits;
     d->op = s.output_positions;
     d->gaps = s.gaps;
+    d->table = s.table;
     d->out = s.outputs;
     d->n_bytes = s.n_bytes;
     d->n_elements = s.n_elements;
@@ -596,6 +666,7 @@ int ecf8_decode(const uint8_t* luts, const uint8_t* encoded, const uint8_t* pack
     s.n_gap_bytes = n_gap_bytes;
     s.outputs = outputs;
     s.n_elements = n_elements;
+    s.table = nullptr;
     return ecf8::launch<1>(&s, 1, (cudaStream_t)cuda_stream);
 }
 
@@ -615,6 +686,19 @@ int ecf8_decode_batch(const ecf8_stream* streams, int n_streams, int threads_per
         st = ecf8::launch<ECF8_MAX_BATCH>(streams + i, n, (cudaStream_t)cuda_stream);
         if (st != ECF8_OK) return st;
     }
+    return ECF8_OK;
+}
+
+int ecf8_build_table(const uint8_t* luts, int n_luts, uint32_t* table, void* cuda_stream) {
+    if (n_luts < 2 || n_luts > ECF8_MAX_LUTS || !luts || !table) return ECF8_ERR_INVALID_ARGUMENT;
+    if (!ecf8::aligned(table, 16)) return ECF8_ERR_INVALID_ARGUMENT;
+    ecf8::DeviceInfo info;
+    int st = ecf8::device_info(&info);
+    if (st != ECF8_OK) return st;
+    ecf8::build_table_kernel<<<1, ecf8::kThreads, sizeof(ecf8::Smem), (cudaStream_t)cuda_stream>>>(luts, n_luts,
+                                                                                                  table);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return ecf8::cuda_fail(e);
     return ECF8_OK;
 }
 

@@ -87,42 +87,85 @@ def _check_u8(t, name, device):
         raise ValueError(f"{name} must be contiguous")
 
 
+def build_decode_table(luts, stream=None):
+    """The stream's 4096-entry multi-symbol decode table (int32 tensor on the
+    LUTs' device), derived from its LUTs by ecf8_build_table.  It depends on
+    the LUTs only: build it once per stream and pass it to every decode."""
+    device = luts.device
+    _check_u8(luts, "luts", device)
+    if device.type != "cuda":
+        raise ValueError("the decode table is built on a CUDA device")
+    table = torch.empty(4096, dtype=torch.int32, device=device)
+    with torch.cuda.device(device):
+        s = stream if stream is not None else torch.cuda.current_stream(device)
+        st = _lib.lib().ecf8_build_table(luts.data_ptr(), luts.shape[0], table.data_ptr(), s.cuda_stream)
+    _lib.check(st, "ecf8_build_table")
+    return table
+
+
+def _stream_struct(s, out, table=None):
+    n = s["packed_other_4bits"].numel() * 2
+    return _lib.Ecf8Stream(
+        s["luts"].data_ptr(), s["luts"].shape[0], 0, s["encoded"].data_ptr(), s["encoded"].numel(),
+        s["packed_other_4bits"].data_ptr(), s["output_positions"].data_ptr(),
+        s["output_positions"].numel() * s["output_positions"].element_size() // 8,
+        s["gaps"].data_ptr(), s["gaps"].numel() * s["gaps"].element_size(), out.data_ptr(), n,
+        table.data_ptr() if table is not None else None)
+
+
+def _check_stream(s, out, device, table=None):
+    for name in STREAM_BUFFERS:
+        _check_u8(s[name], name, device)
+    _check_u8(out, "out", device)
+    if s["luts"].dim() != 2 or s["luts"].shape[1] != 256:
+        raise ValueError("luts must have shape (n_luts, 256)")
+    n = s["packed_other_4bits"].numel() * 2
+    if out.numel() * out.element_size() < n:
+        raise ValueError(f"out holds {out.numel() * out.element_size()} bytes, the stream has {n} elements")
+    if table is not None:
+        _check_u8(table, "table", device)
+        if table.numel() * table.element_size() != 4096 * 4:
+            raise ValueError("a decode table has 4096 32-bit entries")
+
+
 def decode_stream(luts, encoded, packed_other_4bits, output_positions, gaps, out=None,
-                  threads_per_block=512, bytes_per_thread=8, stream=None):
+                  threads_per_block=512, bytes_per_thread=8, stream=None, table=None):
     """Decodes one ECF8 stream (the five buffers a compressed block holds) into
     `out` (e4m3 or uint8, n = 2 * packed_other_4bits.numel() elements;
-    allocated if None).  Asynchronous on `stream` (default: the current
-    stream of the buffers' device).  Returns `out`."""
+    allocated if None).  `table` is the stream's prepared decode table
+    (build_decode_table), or None to derive it inside the kernel.
+    Asynchronous on `stream` (default: the current stream of the buffers'
+    device).  Returns `out`."""
     device = encoded.device
     if device.type != "cuda":
         raise ValueError("ECF8 decode runs on a CUDA device; move the stream buffers there first")
     n = packed_other_4bits.numel() * 2
     if out is None:
         out = torch.empty(n, dtype=torch.float8_e4m3fn, device=device)
-    for t, name in ((luts, "luts"), (encoded, "encoded"), (packed_other_4bits, "packed_other_4bits"),
-                    (output_positions, "output_positions"), (gaps, "gaps"), (out, "out")):
-        _check_u8(t, name, device)
-    if out.numel() * out.element_size() < n:
-        raise ValueError(f"out holds {out.numel()} elements, the stream has {n}")
-    if luts.dim() != 2 or luts.shape[1] != 256:
-        raise ValueError("luts must have shape (n_luts, 256)")
-    n_op = output_positions.numel() * output_positions.element_size() // 8
+    s = {"luts": luts, "encoded": encoded, "packed_other_4bits": packed_other_4bits,
+         "output_positions": output_positions, "gaps": gaps}
+    _check_stream(s, out, device, table)
     L = _lib.lib()
     with torch.cuda.device(device):
-        s = stream if stream is not None else torch.cuda.current_stream(device)
-        st = L.ecf8_decode(luts.data_ptr(), encoded.data_ptr(), packed_other_4bits.data_ptr(),
-                           output_positions.data_ptr(), gaps.data_ptr(), out.data_ptr(),
-                           luts.shape[0], encoded.numel(), n, n_op,
-                           gaps.numel() * gaps.element_size(), threads_per_block, bytes_per_thread,
-                           s.cuda_stream)
+        cs = stream if stream is not None else torch.cuda.current_stream(device)
+        if table is None:
+            st = L.ecf8_decode(luts.data_ptr(), encoded.data_ptr(), packed_other_4bits.data_ptr(),
+                               output_positions.data_ptr(), gaps.data_ptr(), out.data_ptr(),
+                               luts.shape[0], encoded.numel(), n,
+                               output_positions.numel() * output_positions.element_size() // 8,
+                               gaps.numel() * gaps.element_size(), threads_per_block, bytes_per_thread,
+                               cs.cuda_stream)
+        else:
+            arr = (_lib.Ecf8Stream * 1)(_stream_struct(s, out, table))
+            st = L.ecf8_decode_batch(arr, 1, threads_per_block, bytes_per_thread, cs.cuda_stream)
     _lib.check(st, "ecf8_decode")
     return out
 
 
 def decode_streams(streams, outs, threads_per_block=512, bytes_per_thread=8, stream=None):
     """Decodes several streams with one persistent launch per 128 streams.
-    `streams` is a list of dicts with the five stream buffers; `outs` the
-    matching output tensors.  All on one device."""
+    `streams` is a list of dicts with the five stream buffers (and optionally
+    "decode_table"); `outs` the matching output tensors.  All on one device."""
     if len(streams) != len(outs):
         raise ValueError("one output per stream")
     if not streams:
@@ -130,17 +173,9 @@ def decode_streams(streams, outs, threads_per_block=512, bytes_per_thread=8, str
     device = streams[0]["encoded"].device
     arr = (_lib.Ecf8Stream * len(streams))()
     for i, (s, o) in enumerate(zip(streams, outs)):
-        for name in STREAM_BUFFERS:
-            _check_u8(s[name], name, device)
-        _check_u8(o, "out", device)
-        n = s["packed_other_4bits"].numel() * 2
-        if o.numel() * o.element_size() < n:
-            raise ValueError("output too small")
-        arr[i] = _lib.Ecf8Stream(
-            s["luts"].data_ptr(), s["luts"].shape[0], 0, s["encoded"].data_ptr(), s["encoded"].numel(),
-            s["packed_other_4bits"].data_ptr(), s["output_positions"].data_ptr(),
-            s["output_positions"].numel() * s["output_positions"].element_size() // 8,
-            s["gaps"].data_ptr(), s["gaps"].numel(), o.data_ptr(), n)
+        table = s.get("decode_table")
+        _check_stream(s, o, device, table)
+        arr[i] = _stream_struct(s, o, table)
     L = _lib.lib()
     with torch.cuda.device(device):
         cs = stream if stream is not None else torch.cuda.current_stream(device)
@@ -221,8 +256,15 @@ def get_hook(threads_per_block, bytes_per_thread):
         n_elements = module.packed_other_4bits.numel() * 2
         device = module.encoded.device
         reconstructed = TensorManager.get_tensor(device, n_elements)
+        # The decode table depends on the LUTs only: derived on the first
+        # decode on a device and kept as a non-persistent buffer (it is not
+        # part of the checkpoint).
+        table = getattr(module, "ecf8_decode_table", None)
+        if table is None or table.device != device:
+            table = build_decode_table(module.luts)
+            module.register_buffer("ecf8_decode_table", table, persistent=False)
         decode_stream(module.luts, module.encoded, module.packed_other_4bits, module.output_positions,
-                      module.gaps, reconstructed, threads_per_block, bytes_per_thread)
+                      module.gaps, reconstructed, threads_per_block, bytes_per_thread, table=table)
         inject_weights(module, reconstructed)
 
     return decode_hook
@@ -494,9 +536,11 @@ class HostStreamDecoder:
             self.slots[i] = slot
         return slot, need
 
-    def decode(self, streams, outs):
+    def decode(self, streams, outs, tables=None):
         """streams: list of dicts with the five buffers (host tensors);
-        outs: matching host uint8/e4m3 tensors.  Returns when all are done."""
+        outs: matching host uint8/e4m3 tensors; tables: optional prepared
+        decode tables (device tensors, build_decode_table).  Returns when all
+        are done."""
         for j, (s, o) in enumerate(zip(streams, outs)):
             i = j % self.depth
             slot, need = self._slot(i, s)
@@ -515,7 +559,8 @@ class HostStreamDecoder:
             n = need["out"]
             out_dev = slot["out"][:n]
             decode_stream(views["luts"].view(s["luts"].shape), views["encoded"], views["packed_other_4bits"],
-                          views["output_positions"], views["gaps"], out_dev, stream=self.s_dec)
+                          views["output_positions"], views["gaps"], out_dev, stream=self.s_dec,
+                          table=tables[j] if tables is not None else None)
             ev_dec = torch.cuda.Event()
             ev_dec.record(self.s_dec)
             self.s_out.wait_event(ev_dec)

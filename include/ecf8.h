@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ECF8_ABI_VERSION 1
+#define ECF8_ABI_VERSION 2
 
 /* Status codes. */
 #define ECF8_OK 0
@@ -61,6 +61,7 @@ typedef struct ecf8_stream {
     int64_t n_gap_bytes;
     uint8_t* outputs;
     int64_t n_elements;
+    const uint32_t* table; /* from ecf8_build_table(), or NULL (derived in-kernel) */
 } ecf8_stream;
 
 /*
@@ -88,6 +89,18 @@ int ecf8_decode(const uint8_t* luts, const uint8_t* encoded,
                 int64_t n_elements, int64_t n_output_positions,
                 int64_t n_gap_bytes, int threads_per_block,
                 int bytes_per_thread, void* cuda_stream);
+
+/*
+ * Derives a stream's 4096-entry multi-symbol decode table (16 KB, 16-byte
+ * aligned device memory) from its LUTs, asynchronously on cuda_stream.  The
+ * table depends on the LUTs only, so it can be built once when a stream is
+ * loaded and passed in ecf8_stream.table to every later decode; decodes
+ * without it derive the table inside the kernel.  Corresponds to the
+ * per-block set-up the reference loader does once
+ * (dfloat/run/run.py:453-458, shared_mem_size).
+ */
+int ecf8_build_table(const uint8_t* luts, int n_luts, uint32_t* table,
+                     void* cuda_stream);
 
 /*
  * Decodes n_streams independent streams with one persistent launch.  Stands

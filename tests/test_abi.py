@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.ecf8_abi_version() == 1
+    assert lib.ecf8_abi_version() == 2
     assert lib.ecf8_status_string(0) == b"ok"
     assert b"invalid" in lib.ecf8_status_string(1)
     assert lib.ecf8_last_cuda_error() == 0
@@ -46,7 +46,7 @@ def test_abi_version_and_status_strings(lib):
 
 def test_stream_struct_layout_matches_header():
     from ecf8_b200._lib import Ecf8Stream
-    assert ctypes.sizeof(Ecf8Stream) == 88
+    assert ctypes.sizeof(Ecf8Stream) == 96
     assert Ecf8Stream.outputs.offset == 72
 
 
@@ -78,7 +78,7 @@ def test_empty_stream_is_a_no_op(lib):
 def test_batch_rejects_bad_arguments(lib):
     from ecf8_b200._lib import Ecf8Stream
     arr = (Ecf8Stream * 1)()
-    arr[0] = Ecf8Stream(1, 1, 0, 1, 4096, 1, 8, 2, 1, 256, 1, 1000)  # n_luts = 1
+    arr[0] = Ecf8Stream(1, 1, 0, 1, 4096, 1, 8, 2, 1, 256, 1, 1000, None)  # n_luts = 1
     assert lib.ecf8_decode_batch(arr, 1, 512, 8, None) == 1
     assert lib.ecf8_decode_batch(arr, 1, 1024, 8, None) == 2
     assert lib.ecf8_decode_batch(None, 0, 512, 8, None) == 0

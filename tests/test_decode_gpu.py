@@ -217,3 +217,48 @@ def test_full_qwen3_8b_layer_round_trip(cuda_device):
     out2 = decode_stream(c["luts"], c["encoded"], c["packed_other_4bits"], c["output_positions"], c["gaps"],
                          out)
     assert torch.equal(out2.view(torch.uint8), flat.view(torch.uint8))
+
+
+@pytest.mark.parametrize("name", golden_names())
+def test_golden_streams_with_prepared_table(cuda_device, name):
+    """A table prepared once by ecf8_build_table decodes exactly like the
+    table the kernel derives itself."""
+    from ecf8_b200.run import build_decode_table, decode_stream
+    s = load_golden(name)
+    d = to_device(s, cuda_device)
+    table = build_decode_table(d["luts"])
+    n = s["fp8"].size
+    buf = torch.full((n + 64,), GUARD, dtype=torch.uint8, device=cuda_device)
+    decode_stream(d["luts"], d["encoded"], d["packed_other_4bits"], d["output_positions"], d["gaps"],
+                  buf[32:32 + n], table=table)
+    derived, _ = decode_guarded(d, n, cuda_device)
+    b = buf.cpu().numpy()
+    assert np.all(b[:32] == GUARD) and np.all(b[32 + n:] == GUARD)
+    assert np.array_equal(b[32:32 + n], s["fp8"])
+    assert np.array_equal(b[32:32 + n], derived)
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_random_streams_with_prepared_table(cuda_device, oracle_mod, seed):
+    from ecf8_b200.run import build_decode_table, decode_stream
+    rng = np.random.default_rng(5000 + seed)
+    s = random_stream(oracle_mod, rng)
+    d = to_device(s, cuda_device)
+    out = decode_stream(d["luts"], d["encoded"], d["packed_other_4bits"], d["output_positions"], d["gaps"],
+                        table=build_decode_table(d["luts"]))
+    assert np.array_equal(out.view(torch.uint8).cpu().numpy(), s["fp8"])
+
+
+def test_batch_mixing_prepared_and_derived_tables(cuda_device):
+    from ecf8_b200.run import build_decode_table, decode_streams
+    names = golden_names()
+    ss = [load_golden(n) for n in names]
+    ds = [to_device(s, cuda_device) for s in ss]
+    for i, d in enumerate(ds):
+        if i % 2 == 0:
+            d["decode_table"] = build_decode_table(d["luts"])
+    outs = [torch.zeros(s["fp8"].size, dtype=torch.uint8, device=cuda_device) for s in ss]
+    decode_streams(ds, outs)
+    torch.cuda.synchronize()
+    for n, s, o in zip(names, ss, outs):
+        assert np.array_equal(o.cpu().numpy(), s["fp8"]), n
