@@ -112,15 +112,16 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // 16-byte aligned, else plain byte loads.
 __device__ __forceinline__ void stage(uint8_t* dst, const uint8_t* src, long long lo, int size, long long limit,
                                       bool async_ok) {
+    const long long vl = limit - lo;
+    const int valid = vl < 0 ? 0 : (vl > size ? size : (int)vl);  // bytes of the range that exist
+    const uint8_t* s = src + lo;
     for (int i = threadIdx.x * 16; i < size; i += kThreads * 16) {
-        const long long a = lo + i;
-        long long v = limit - a;
-        v = v < 0 ? 0 : (v > 16 ? 16 : v);
+        const int v = min(max(valid - i, 0), 16);
         if (async_ok) {
-            cp_async16(dst + i, v ? src + a : src, (uint32_t)v);
+            cp_async16(dst + i, v ? s + i : src, (uint32_t)v);
         } else {
 #pragma unroll
-            for (int k = 0; k < 16; ++k) dst[i + k] = k < v ? __ldg(src + a + k) : (uint8_t)0;
+            for (int k = 0; k < 16; ++k) dst[i + k] = k < v ? __ldg(s + i + k) : (uint8_t)0;
         }
     }
 }
@@ -279,45 +280,72 @@ __device__ void setup_stream(Smem& S, const DevStream& d) {
 // through a 64-bit accumulator (ah:al) into the thread's shared-memory slot,
 // eight at a time.  Returns the number of codes that start in run bits
 // [gap, 128) -- the two windows' counts of decode.cu:65-112 together.
+//
+// The inner loop takes table steps only and has no divergent branches: the
+// slot store is unconditional (a partly filled word is rewritten until it is
+// full) and only the store pointer advance depends on the fill.  It leaves
+// for a code longer than the table width or at the end of a 64-bit half.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t* slot, uint32_t w0, uint32_t w1,
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+__device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
+    asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, uint32_t w0, uint32_t w1,
                                                uint32_t w2, uint32_t w3, uint32_t w4, uint32_t gap) {
+    const uint32_t tab_s = (uint32_t)__cvta_generic_to_shared(S.tab);
     uint32_t h = __funnelshift_l(w1, w0, gap);
     uint32_t m = __funnelshift_l(w2, w1, gap);
     uint32_t x = w2 << gap;
-    uint32_t p = gap, ah = 0, al = 0, m4 = 0, second = 0;
-    uint32_t* sp = slot;
+    uint32_t p = gap, ah = 0, al = 0, m4 = 0, second = 0, sa = slot_s;
     uint32_t e, b;
     for (;;) {
-        e = S.tab[h >> (32 - kTabBits)];
-        b = (e >> 8) & 15u;
-        if (b == 0) {  // no complete code within the table width: two-level LUT
+        do {
+            e = lds32(tab_s + ((h >> (32 - kTabBits)) << 2));
+            b = (e >> 8) & 15u;
+            if (b == 0) break;  // no complete code within the table width
+            ah = __funnelshift_l(al, ah, e);  // append e's symbols; shift = e & 31 = 4 x count
+            al = __funnelshift_l(e, al, e);
+            m4 += e & 31u;
+            const bool full = m4 >= 32;
+            m4 = full ? m4 - 32 : m4;
+            sts32(sa, __funnelshift_r(al, ah, m4));
+            sa = full ? sa + 4 : sa;
+            h = __funnelshift_l(m, h, b);
+            m = __funnelshift_l(x, m, b);
+            x <<= b;
+            p += b;
+        } while (p < 64);
+        if (b == 0) {  // two-level LUT (decode.cu:86-91)
             const uint32_t sym = lut_symbol(S, h);
             b = code_length(S, sym);
             e = ((sym & 15u) << 28) | 4u;
+            ah = __funnelshift_l(al, ah, e);
+            al = __funnelshift_l(e, al, e);
+            m4 += 4;
+            const bool full = m4 >= 32;
+            m4 = full ? m4 - 32 : m4;
+            sts32(sa, __funnelshift_r(al, ah, m4));
+            sa = full ? sa + 4 : sa;
+            h = __funnelshift_l(m, h, b);
+            m = __funnelshift_l(x, m, b);
+            x <<= b;
+            p += b;
+            if (p < 64) continue;
         }
-        ah = __funnelshift_l(al, ah, e);  // append e's symbols; shift = e & 31 = 4 x count
-        al = __funnelshift_l(e, al, e);
-        m4 += e & 31u;
-        if (m4 >= 32) {
-            m4 -= 32;
-            *sp++ = __funnelshift_r(al, ah, m4);
-        }
-        h = __funnelshift_l(m, h, b);
-        m = __funnelshift_l(x, m, b);
-        x <<= b;
-        p += b;
-        if (p >= 64) {
-            if (second) break;
-            second = 1;  // continue in the second window: bits [64, 160) of the run
-            p -= 64;
-            h = __funnelshift_l(w3, w2, p);
-            m = __funnelshift_l(w4, w3, p);
-            x = w4 << p;
-        }
+        if (second) break;
+        second = 1;  // continue in the second window: bits [64, 160) of the run
+        p -= 64;
+        h = __funnelshift_l(w3, w2, p);
+        m = __funnelshift_l(w4, w3, p);
+        x = w4 << p;
     }
-    if (m4) *sp = al << (32 - m4);
-    uint32_t n = (uint32_t)(sp - slot) * 8 + (m4 >> 2);
+    if (m4) sts32(sa, al << (32 - m4));
+    uint32_t n = ((sa - slot_s) >> 2) * 8 + (m4 >> 2);
     // The last step may have taken codes that start at or after the run's
     // end; they belong to the next run.
     const uint32_t room = 64 - (p - b);
@@ -424,7 +452,8 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
             r = group_range(B.s[sn], gn);
         }
         cp_async_commit();
-        for (int i = t; i < 2 * n_chunks; i += kThreads) S.obuf[i] = 0;
+        for (int i = t; i < (n_chunks + 1) >> 1; i += kThreads)  // obuf is 16-byte aligned, 4 words a store
+            reinterpret_cast<uint4*>(S.obuf)[i] = make_uint4(0, 0, 0, 0);
 
         // --- decode this thread's window pair ---
         uint32_t* slot = S.slot + t * kSlotWords;
@@ -432,7 +461,8 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
         if (g * kGroupBytes + 16 * t < d.n_bytes) {
             const uint4 raw = *reinterpret_cast<const uint4*>(S.enc[buf] + 16 * t);
             const uint32_t r4 = *reinterpret_cast<const uint32_t*>(S.enc[buf] + 16 * t + 16);
-            count = decode_run(S, slot, __byte_perm(raw.x, 0, 0x0123), __byte_perm(raw.y, 0, 0x0123),
+            count = decode_run(S, (uint32_t)__cvta_generic_to_shared(slot), __byte_perm(raw.x, 0, 0x0123),
+                               __byte_perm(raw.y, 0, 0x0123),
                                __byte_perm(raw.z, 0, 0x0123), __byte_perm(raw.w, 0, 0x0123),
                                __byte_perm(r4, 0, 0x0123), S.gaps[buf][t] >> 4);
         }
@@ -482,19 +512,42 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
 
         // --- merge with sign+mantissa nibbles, 16 elements per store ---
         const uint8_t* pk = S.pack + pofs;
-        for (int c = t; c < n_chunks; c += kThreads) {
-            const uint32_t e0 = 16u * c;
-            const uint2 ew = *reinterpret_cast<const uint2*>(&S.obuf[2 * c]);
-            const uint2 pw = c < kPackChunks ? *reinterpret_cast<const uint2*>(pk + 8 * c)
-                                             : packed8(d, (base >> 1) + 8ull * c);
-            uint4 o;
-            merge8(ew.x, pw.x, o.x, o.y);
-            merge8(ew.y, pw.y, o.z, o.w);
-            uint8_t* dst = d.out + base + e0;
-            if (d.out16 && e0 >= rs && e0 + 16 <= re) {
-                *reinterpret_cast<uint4*>(dst) = o;
-            } else {
-                const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+        // Chunks wholly inside [start, end) are stored 16 bytes at a time; the
+        // group's first and last chunk may be partial (shared with the
+        // neighbouring groups) and are written byte by byte by two threads.
+        const int c_first = rs ? 1 : 0;
+        const int c_end = (int)(re >> 4);  // chunks [c_first, c_end) are full
+        if (d.out16) {
+            for (int c = c_first + t; c < c_end; c += kThreads) {
+                const uint2 ew = *reinterpret_cast<const uint2*>(&S.obuf[2 * c]);
+                const uint2 pw = c < kPackChunks ? *reinterpret_cast<const uint2*>(pk + 8 * c)
+                                                 : packed8(d, (base >> 1) + 8ull * c);
+                uint4 o;
+                merge8(ew.x, pw.x, o.x, o.y);
+                merge8(ew.y, pw.y, o.z, o.w);
+                *reinterpret_cast<uint4*>(d.out + base + 16u * c) = o;
+            }
+        }
+        {
+            // Byte path: partial chunks (threads 0 and 1), and every chunk
+            // when the output is not 16-byte aligned.
+            int c = -1;
+            if (!d.out16) {
+                c = t;
+            } else if (t == 0 && rs) {
+                c = 0;
+            } else if (t == 1 && (re & 15) && (int)(re >> 4) >= c_first) {
+                c = (int)(re >> 4);
+            }
+            for (; c >= 0 && c < n_chunks; c = d.out16 ? -1 : c + kThreads) {
+                const uint32_t e0 = 16u * c;
+                const uint2 ew = *reinterpret_cast<const uint2*>(&S.obuf[2 * c]);
+                const uint2 pw = c < kPackChunks ? *reinterpret_cast<const uint2*>(pk + 8 * c)
+                                                 : packed8(d, (base >> 1) + 8ull * c);
+                uint32_t ow[4];
+                merge8(ew.x, pw.x, ow[0], ow[1]);
+                merge8(ew.y, pw.y, ow[2], ow[3]);
+                uint8_t* dst = d.out + base + e0;
 #pragma unroll
                 for (int k = 0; k < 16; ++k)
                     if (e0 + k >= rs && e0 + k < re) dst[k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
