@@ -5,14 +5,18 @@
 // like the reference kernel dfloat/run/decode.cu:16-211, with a different
 // design:
 //
-//  * Persistent CTAs.  Each CTA of 256 threads walks a contiguous range of
-//    4096-byte groups (one reference thread block's worth of stream), across
-//    one or many streams of a batch.
+//  * Persistent CTAs of three teams.  One CTA of 768 threads per SM holds
+//    one copy of the stream's decode tables in shared memory; each team of
+//    256 threads walks every third 4096-byte group (one reference thread
+//    block's worth of stream) of the CTA's range, synchronising on its own
+//    named barrier, so the teams' phases interleave like separate CTAs.
 //  * Multi-symbol table.  A 4096-entry table indexed by the next 12 stream
-//    bits yields up to five whole symbols, the bits they use and their count.
-//    It is a pure function of the stream's LUTs: ecf8_build_table() derives
-//    it once per stream (at load time) and every CTA copies it into shared
-//    memory; without a prepared table each CTA derives it itself.
+//    bits yields up to five whole symbols, the bits they use and their count,
+//    plus a counter step that advances the bit position, the output nibble
+//    count and the output word address with one add.  It is a pure function
+//    of the stream's LUTs: ecf8_build_table() derives it once per stream (at
+//    load time) and every CTA copies it into shared memory; without a
+//    prepared table each CTA derives it itself.
 //  * Two windows per thread, one decode pass.  Each thread decodes its two
 //    adjacent 64-bit windows as one continuous run (the first window's gap
 //    gives the start) into a private shared-memory slot of nibbles; a
@@ -39,7 +43,9 @@ namespace {
 
 constexpr int kGroupWindows = ECF8_THREADS_PER_BLOCK;   // windows per group (512)
 constexpr int kWindowBytes = ECF8_BYTES_PER_THREAD;     // bytes per window (8)
-constexpr int kThreads = kGroupWindows / 2;             // CTA size: two windows per thread
+constexpr int kTeamThreads = kGroupWindows / 2;         // team size: two windows per thread
+constexpr int kTeams = 3;                               // teams per CTA
+constexpr int kThreads = kTeamThreads * kTeams;         // CTA size
 constexpr int kGroupBytes = kGroupWindows * kWindowBytes;  // 4096
 constexpr int kTabBits = 12;                            // multi-symbol table width
 constexpr int kTabSize = 1 << kTabBits;
@@ -53,22 +59,38 @@ constexpr int kGapStage = kGroupWindows / 2;            // 4 bits per window
 constexpr int kPackChunks = 1024;                       // 16-element chunks whose nibbles are staged
 constexpr int kPackStage = kPackChunks * 8 + 16;        // the rest of a (rare) longer group: global loads
 
+// One team's buffers.
+struct alignas(16) Team {
+    uint32_t slot[kTeamThreads * kSlotWords];  // per-thread decoded nibbles (MSB first)
+    uint32_t obuf[kObufWords];                 // output-ordered exponent nibbles
+    uint8_t enc[2][kEncStage];                 // staged bitstream, double buffered
+    uint8_t gaps[2][kGapStage];                // staged gaps, double buffered
+    uint8_t pack[kPackStage];                  // staged sign+mantissa nibbles
+    uint32_t wsum[kTeamThreads / 32];          // scan: warp totals
+};
+static_assert(offsetof(Team, obuf) % 16 == 0, "obuf must allow 16-byte stores");
+static_assert(offsetof(Team, enc) % 16 == 0 && kEncStage % 16 == 0, "cp.async targets are 16-byte units");
+static_assert(offsetof(Team, gaps) % 16 == 0 && offsetof(Team, pack) % 16 == 0, "cp.async alignment");
+static_assert(sizeof(Team) % 16 == 0, "teams stay 16-byte aligned");
+
 struct alignas(16) Smem {
-    uint32_t tab[kTabSize];                  // multi-symbol entries
-    uint32_t slot[kThreads * kSlotWords];    // per-thread decoded nibbles (MSB first)
-    uint32_t obuf[kObufWords];               // output-ordered exponent nibbles
-    uint8_t enc[2][kEncStage];               // staged bitstream, double buffered
-    uint8_t gaps[2][kGapStage];              // staged gaps, double buffered
-    uint8_t pack[kPackStage];                // staged sign+mantissa nibbles
+    uint2 tab[kTabSize];                     // multi-symbol entries (x: entry, y: counter step)
     uint8_t lut[kLutRows * 256];             // reference LUT rows 0..n_luts-2, zero padded
     uint8_t lens[256];                       // reference LUT last row: code lengths
     uint32_t chg[kLutRows * 8];              // per row: bit b set if entry b != entry b-1
-    uint32_t wsum[kThreads / 32];            // scan: warp totals
+    Team team[kTeams];
 };
-static_assert(offsetof(Smem, obuf) % 16 == 0, "obuf must allow 8-byte vector reads");
-static_assert(offsetof(Smem, enc) % 16 == 0 && kEncStage % 16 == 0, "cp.async targets are 16-byte units");
-static_assert(offsetof(Smem, gaps) % 16 == 0 && offsetof(Smem, pack) % 16 == 0, "cp.async alignment");
-static_assert(offsetof(Smem, slot) % 16 == 0 && offsetof(Smem, tab) % 16 == 0, "vector copies");
+static_assert(offsetof(Smem, team) % 16 == 0 && offsetof(Smem, tab) % 16 == 0, "vector copies");
+
+// Shared-memory layout of build_table_kernel: the decode tables only.
+struct alignas(16) TableSmem {
+    uint2 tab[kTabSize];
+    uint8_t lut[kLutRows * 256];
+    uint8_t lens[256];
+    uint32_t chg[kLutRows * 8];
+};
+static_assert(offsetof(Smem, lut) == offsetof(TableSmem, lut) && offsetof(Smem, chg) == offsetof(TableSmem, chg),
+              "the table functions see the same layout");
 
 struct DevStream {
     const uint8_t* luts;
@@ -111,11 +133,11 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // size is a multiple of 16.  Asynchronous with cp.async when src + lo is
 // 16-byte aligned, else plain byte loads.
 __device__ __forceinline__ void stage(uint8_t* dst, const uint8_t* src, long long lo, int size, long long limit,
-                                      bool async_ok) {
+                                      bool async_ok, int t) {
     const long long vl = limit - lo;
     const int valid = vl < 0 ? 0 : (vl > size ? size : (int)vl);  // bytes of the range that exist
     const uint8_t* s = src + lo;
-    for (int i = threadIdx.x * 16; i < size; i += kThreads * 16) {
+    for (int i = t * 16; i < size; i += kTeamThreads * 16) {
         const int v = min(max(valid - i, 0), 16);
         if (async_ok) {
             cp_async16(dst + i, v ? s + i : src, (uint32_t)v);
@@ -134,14 +156,16 @@ __device__ __forceinline__ void stage(uint8_t* dst, const uint8_t* src, long lon
 // code starts the pattern within 12 bits; the decoder then uses the
 // two-level LUT directly.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t lut_symbol(const Smem& S, uint32_t top) {
+template <class SM>
+__device__ __forceinline__ uint32_t lut_symbol(const SM& S, uint32_t top) {
     // `top` holds the next >= 16 stream bits left-aligned (dfloat/run/decode.cu:86-88).
     uint32_t d = S.lut[top >> 24];
     if (d >= 240) d = S.lut[(256u - d) * 256u + ((top >> 16) & 255u)];
     return d;
 }
 
-__device__ __forceinline__ uint32_t code_length(const Smem& S, uint32_t sym) {
+template <class SM>
+__device__ __forceinline__ uint32_t code_length(const SM& S, uint32_t sym) {
     // decode.cu:91.  A length of 0 can only be met in the bits after the EOF
     // code (the reference would spin there); it advances by one bit.
     uint32_t len = S.lens[sym & 255u];
@@ -149,7 +173,8 @@ __device__ __forceinline__ uint32_t code_length(const Smem& S, uint32_t sym) {
 }
 
 // Bit j set for the end offset of each symbol of entry e (offsets 1..12).
-__device__ __forceinline__ uint32_t entry_ends(const Smem& S, uint32_t e) {
+template <class SM>
+__device__ __forceinline__ uint32_t entry_ends(const SM& S, uint32_t e) {
     const uint32_t c = (e & 31u) >> 2;
     uint32_t pos = 0, mask = 0;
     for (uint32_t i = 0; i < c; ++i) {
@@ -161,7 +186,8 @@ __device__ __forceinline__ uint32_t entry_ends(const Smem& S, uint32_t e) {
 
 // True when LUT row `row` holds one value over the 2^pad entries starting at
 // `lo` (lo is a multiple of 2^pad).
-__device__ __forceinline__ bool row_constant(const Smem& S, int row, uint32_t lo, uint32_t pad) {
+template <class SM>
+__device__ __forceinline__ bool row_constant(const SM& S, int row, uint32_t lo, uint32_t pad) {
     if (pad == 0) return true;
     const uint32_t* c = S.chg + row * 8;
     if (pad <= 5) {
@@ -177,7 +203,8 @@ __device__ __forceinline__ bool row_constant(const Smem& S, int row, uint32_t lo
 // whole code range maps to it in the LUTs.  Every code of the table is one;
 // bit patterns of the EOF code or of unused code space are not (there the
 // LUT's carry-forward answer depends on bits past the returned length).
-__device__ __forceinline__ bool real_code(const Smem& S, uint32_t v, uint32_t& sym, uint32_t& len) {
+template <class SM>
+__device__ __forceinline__ bool real_code(const SM& S, uint32_t v, uint32_t& sym, uint32_t& len) {
     const uint32_t b1 = v >> 8;
     const uint32_t d = S.lut[b1];
     if (d < 240) {
@@ -200,21 +227,23 @@ __device__ __forceinline__ bool real_code(const Smem& S, uint32_t v, uint32_t& s
 }
 
 // Copies the stream's LUT rows into shared memory (all threads; ends with a barrier).
-__device__ void load_luts(Smem& S, const DevStream& d) {
+template <class SM>
+__device__ void load_luts(SM& S, const DevStream& d) {
     const int t = threadIdx.x;
-    for (int i = t; i < kLutRows * 256; i += kThreads) {
+    for (int i = t; i < kLutRows * 256; i += (int)blockDim.x) {
         const int row = i >> 8;
         S.lut[i] = (row < d.n_luts - 1) ? __ldg(d.luts + i) : (uint8_t)0;
     }
-    for (int i = t; i < 256; i += kThreads) S.lens[i] = __ldg(d.luts + (d.n_luts - 1) * 256 + i);
+    for (int i = t; i < 256; i += (int)blockDim.x) S.lens[i] = __ldg(d.luts + (d.n_luts - 1) * 256 + i);
     __syncthreads();
 }
 
 // Derives the multi-symbol table from the LUTs in shared memory (all threads).
-__device__ void derive_table(Smem& S) {
+template <class SM>
+__device__ void derive_table(SM& S) {
     const int t = threadIdx.x;
     // Change bitmaps, one ballot per 32 entries (rows are 256 = 8 x 32 wide).
-    for (int i = t; i < kLutRows * 256; i += kThreads) {
+    for (int i = t; i < kLutRows * 256; i += (int)blockDim.x) {
         const bool change = (i & 255) && S.lut[i] != S.lut[i - 1];
         const uint32_t m = __ballot_sync(0xffffffffu, change);
         if ((t & 31) == 0) S.chg[i >> 5] = m;
@@ -228,7 +257,7 @@ __device__ void derive_table(Smem& S) {
             pos += len;
             ++c;
         }
-        S.tab[0] = syms | (pos << 8) | (4 * c);
+        S.tab[0].x = syms | (pos << 8) | (4 * c);
     }
     __syncthreads();
     // Entry x from entry y = (x << l) & 0xfff, where l is x's first code length:
@@ -237,13 +266,13 @@ __device__ void derive_table(Smem& S) {
     // trailing-zero count, one round per count.
     for (int tz = kTabBits - 1; tz >= 0; --tz) {
         const int n = 1 << (kTabBits - 1 - tz);
-        for (int j = t; j < n; j += kThreads) {
+        for (int j = t; j < n; j += (int)blockDim.x) {
             const uint32_t x = (uint32_t)(2 * j + 1) << tz;
             uint32_t sym, len, ent = 0;
             if (real_code(S, x << 4, sym, len) && len <= (uint32_t)kTabBits) {
                 uint32_t kept = 0, endk = 0, rest = 0;
                 if (len < (uint32_t)kTabBits) {
-                    const uint32_t ey = S.tab[(x << len) & (kTabSize - 1)];
+                    const uint32_t ey = S.tab[(x << len) & (kTabSize - 1)].x;
                     const uint32_t ends = entry_ends(S, ey);
                     kept = min(__popc(ends & ((2u << (kTabBits - len)) - 1u)), kMaxSymsPerEntry - 1);
                     if (kept) {
@@ -253,43 +282,59 @@ __device__ void derive_table(Smem& S) {
                 }
                 ent = ((sym & 15u) << 28) | rest | ((len + endk) << 8) | (4 * (1 + kept));
             }
-            S.tab[x] = ent;
+            S.tab[x].x = ent;
         }
         __syncthreads();
     }
 }
 
+// Counter step of a table entry (see decode_run): (bits << 24) | 4 x count.  An
+// entry without a complete code (bits 0) becomes all-zero, which sends the
+// decode to the two-level LUT, whatever the rest of the entry holds.
+__device__ __forceinline__ uint2 expand_entry(uint32_t e) {
+    const uint32_t b = (e >> 8) & 15u;
+    return b ? make_uint2(e, (b << 24) | (e & 31u)) : make_uint2(0u, 0u);
+}
+
 // LUTs plus the table: copied when prepared, derived otherwise (ends with a barrier).
-__device__ void setup_stream(Smem& S, const DevStream& d) {
+template <class SM>
+__device__ void setup_stream(SM& S, const DevStream& d) {
     if (d.table) {
         const uint4* src = reinterpret_cast<const uint4*>(d.table);
         uint4* dst = reinterpret_cast<uint4*>(S.tab);
-        for (int i = threadIdx.x; i < kTabSize / 4; i += kThreads) dst[i] = __ldg(src + i);
+        for (int i = threadIdx.x; i < kTabSize / 4; i += (int)blockDim.x) {
+            const uint4 q = __ldg(src + i);
+            const uint2 a = expand_entry(q.x), b = expand_entry(q.y), c = expand_entry(q.z), e = expand_entry(q.w);
+            dst[2 * i] = make_uint4(a.x, a.y, b.x, b.y);
+            dst[2 * i + 1] = make_uint4(c.x, c.y, e.x, e.y);
+        }
         load_luts(S, d);
     } else {
         load_luts(S, d);
         derive_table(S);
+        for (int i = threadIdx.x; i < kTabSize; i += (int)blockDim.x) S.tab[i] = expand_entry(S.tab[i].x);
+        __syncthreads();
     }
 }
 
 // ---------------------------------------------------------------------------
 // Run decode.  A thread's run is its two adjacent windows: stream bits
 // [gap, 128) of the pair, with the 32 bits after the pair as look-ahead.  The
-// next 96 bits sit left-aligned in the shift register (h:m:x); p is the bit
-// offset of its top within the current 64-bit half.  Decoded nibbles go
-// through a 64-bit accumulator (ah:al) into the thread's shared-memory slot,
-// eight at a time.  Returns the number of codes that start in run bits
+// next 160 - p bits sit left-aligned in the shift register h:m:x:y:z.
+// Decoded nibbles go through a 64-bit accumulator (ah:al) into the thread's
+// shared-memory slot.  Returns the number of codes that start in run bits
 // [gap, 128) -- the two windows' counts of decode.cu:65-112 together.
 //
-// The inner loop takes table steps only and has no divergent branches: the
-// slot store is unconditional (a partly filled word is rewritten until it is
-// full) and only the store pointer advance depends on the fill.  It leaves
-// for a code longer than the table width or at the end of a 64-bit half.
+// One counter K carries all of a step's bookkeeping: bits 4..0 are the
+// nibble bits of the open slot word, bits 23..5 that word's shared address / 4
+// (carries out of bit 4 advance it), bits 31..24 the bit position p.  A table
+// entry's y word is the counter step, so one add does it.  The slot store is
+// unconditional (a partly filled word is rewritten until it is full).  Codes
+// longer than the table width take the two-level LUT inside the loop, so that
+// a warp stays converged.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
+__device__ __forceinline__ void lds64(uint32_t a, uint32_t& lo, uint32_t& hi) {
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(lo), "=r"(hi) : "r"(a));
 }
 __device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
     asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
@@ -300,61 +345,44 @@ __device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, u
     const uint32_t tab_s = (uint32_t)__cvta_generic_to_shared(S.tab);
     uint32_t h = __funnelshift_l(w1, w0, gap);
     uint32_t m = __funnelshift_l(w2, w1, gap);
-    uint32_t x = w2 << gap;
-    uint32_t p = gap, ah = 0, al = 0, m4 = 0, second = 0, sa = slot_s;
-    uint32_t e, b;
-    for (;;) {
-        do {
-            e = lds32(tab_s + ((h >> (32 - kTabBits)) << 2));
-            b = (e >> 8) & 15u;
-            if (b == 0) break;  // no complete code within the table width
-            ah = __funnelshift_l(al, ah, e);  // append e's symbols; shift = e & 31 = 4 x count
-            al = __funnelshift_l(e, al, e);
-            m4 += e & 31u;
-            const bool full = m4 >= 32;
-            m4 = full ? m4 - 32 : m4;
-            sts32(sa, __funnelshift_r(al, ah, m4));
-            sa = full ? sa + 4 : sa;
-            h = __funnelshift_l(m, h, b);
-            m = __funnelshift_l(x, m, b);
-            x <<= b;
-            p += b;
-        } while (p < 64);
-        if (b == 0) {  // two-level LUT (decode.cu:86-91)
+    uint32_t x = __funnelshift_l(w3, w2, gap);
+    uint32_t y = __funnelshift_l(w4, w3, gap);
+    uint32_t z = w4 << gap;
+    uint32_t K = (gap << 24) | ((slot_s >> 2) << 5);
+    uint32_t ah = 0, al = 0, elo, ehi;
+#pragma unroll 1
+    do {
+        const uint32_t sa = (K >> 3) & 0x1ffffcu;
+        lds64(tab_s + ((h >> (32 - kTabBits)) << 3), elo, ehi);
+        if (__builtin_expect(elo == 0, 0)) {  // no complete code within the table width (decode.cu:86-91)
             const uint32_t sym = lut_symbol(S, h);
-            b = code_length(S, sym);
-            e = ((sym & 15u) << 28) | 4u;
-            ah = __funnelshift_l(al, ah, e);
-            al = __funnelshift_l(e, al, e);
-            m4 += 4;
-            const bool full = m4 >= 32;
-            m4 = full ? m4 - 32 : m4;
-            sts32(sa, __funnelshift_r(al, ah, m4));
-            sa = full ? sa + 4 : sa;
-            h = __funnelshift_l(m, h, b);
-            m = __funnelshift_l(x, m, b);
-            x <<= b;
-            p += b;
-            if (p < 64) continue;
+            elo = ((sym & 15u) << 28) | 4u;
+            ehi = (min(code_length(S, sym), 32u) << 24) | 4u;
         }
-        if (second) break;
-        second = 1;  // continue in the second window: bits [64, 160) of the run
-        p -= 64;
-        h = __funnelshift_l(w3, w2, p);
-        m = __funnelshift_l(w4, w3, p);
-        x = w4 << p;
-    }
-    if (m4) sts32(sa, al << (32 - m4));
-    uint32_t n = ((sa - slot_s) >> 2) * 8 + (m4 >> 2);
+        ah = __funnelshift_l(al, ah, elo);  // append the entry's symbols; shift = elo & 31 = 4 x count
+        al = __funnelshift_l(elo, al, elo);
+        K += ehi;
+        sts32(sa, __funnelshift_r(al, ah, K));
+        const uint32_t b = ehi >> 24;
+        h = __funnelshift_l(m, h, b);
+        m = __funnelshift_l(x, m, b);
+        x = __funnelshift_l(y, x, b);
+        y = __funnelshift_l(z, y, b);
+        z <<= b;
+    } while (K < (128u << 24));
+    const uint32_t m4 = K & 31u;
+    const uint32_t words = ((K >> 5) & 0x7ffffu) - (slot_s >> 2);
+    if (m4) sts32(slot_s + 4 * words, al << (32 - m4));
+    uint32_t n = words * 8 + (m4 >> 2);
     // The last step may have taken codes that start at or after the run's
     // end; they belong to the next run.
-    const uint32_t room = 64 - (p - b);
+    const uint32_t room = 128u - ((K >> 24) - (ehi >> 24));
     if (room < (uint32_t)kTabBits) {
-        const uint32_t c = (e & 31u) >> 2;
+        const uint32_t c = (elo & 31u) >> 2;
         uint32_t start = 0, keep = 0;
         for (uint32_t i = 0; i < c; ++i) {
             keep += start < room;
-            start += code_length(S, (e >> (28 - 4 * i)) & 15u);
+            start += code_length(S, (elo >> (28 - 4 * i)) & 15u);
         }
         n -= c - keep;
     }
@@ -387,9 +415,13 @@ __device__ __forceinline__ GroupRange group_range(const DevStream& d, long long 
     return {start, end};
 }
 
-__device__ __forceinline__ void stage_window_bytes(Smem& S, int buf, const DevStream& d, long long g) {
-    stage(S.enc[buf], d.encoded, g * kGroupBytes, kEncStage, d.n_bytes, d.async_ok);
-    stage(S.gaps[buf], d.gaps, g * kGapStage, kGapStage, g * kGapStage + kGapStage, d.async_ok);
+__device__ __forceinline__ void stage_window_bytes(Team& T, int buf, const DevStream& d, long long g, int t) {
+    stage(T.enc[buf], d.encoded, g * kGroupBytes, kEncStage, d.n_bytes, d.async_ok, t);
+    stage(T.gaps[buf], d.gaps, g * kGapStage, kGapStage, g * kGapStage + kGapStage, d.async_ok, t);
+}
+
+__device__ __forceinline__ void team_sync(int team) {
+    asm volatile("bar.sync %0, %1;" ::"r"(team + 1), "n"(kTeamThreads) : "memory");
 }
 
 __device__ __forceinline__ int find_stream(const DevStream* s, int from, long long w) {
@@ -408,63 +440,50 @@ __device__ __forceinline__ uint2 packed8(const DevStream& d, unsigned long long 
     return make_uint2(b[0] | b[1] << 8 | b[2] << 16 | b[3] << 24, b[4] | b[5] << 8 | b[6] << 16 | b[7] << 24);
 }
 
-template <int MAXS>
-__global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_constant__ Batch<MAXS> B) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    Smem& S = *reinterpret_cast<Smem*>(smem_raw);
-    const int t = threadIdx.x;
+// One team decodes groups g0, g0 + kTeams, ... below g_end of stream d.  t is
+// the thread's index in the team; the team's barrier is named barrier team+1.
+__device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, long long g0, long long g_end, int team,
+                              int t) {
+    if (g0 >= g_end) return;
     const int lane = t & 31, warp = t >> 5;
-    const long long total = B.total_groups;
-    const long long lo = (long long)blockIdx.x * total / gridDim.x;
-    const long long hi = (long long)(blockIdx.x + 1) * total / gridDim.x;
-    if (lo >= hi) return;
-
-    int si = find_stream(B.s, 0, lo);
-    stage_window_bytes(S, 0, B.s[si], lo - B.s[si].group_begin);
+    uint32_t* slot = T.slot + t * kSlotWords;
+    const uint32_t slot_s = (uint32_t)__cvta_generic_to_shared(slot);
+    stage_window_bytes(T, 0, d, g0, t);
     cp_async_commit();
-    GroupRange r = group_range(B.s[si], lo - B.s[si].group_begin);
-    setup_stream(S, B.s[si]);
-
-    for (long long w = lo; w < hi; ++w) {
-        const int buf = (int)((w - lo) & 1);
-        const DevStream& d = B.s[si];
-        const long long g = w - d.group_begin;
+    GroupRange r = group_range(d, g0);
+    int buf = 0;
+    for (long long g = g0; g < g_end; g += kTeams, buf ^= 1) {
         const unsigned long long start = r.start, end = r.end;
         const unsigned long long base = start & ~15ull;
         const uint32_t rs = (uint32_t)(start - base), re = (uint32_t)(end - base);  // range rel. to base
         const int n_chunks = (int)((re + 15) >> 4);
 
         cp_async_wait<0>();  // this group's window bytes
-        __syncthreads();     // ... visible; previous group's merge done with pack / obuf / slots
+        team_sync(team);     // ... visible; previous group's merge done with pack / obuf / slots
 
         // Stage this group's packed nibbles and the next group's window bytes;
         // fetch the next group's output range.
         const long long p0 = (long long)(base >> 1) & ~15ll;
         const uint32_t pofs = (uint32_t)((base >> 1) - p0);  // 0 or 8
         const int staged = n_chunks < kPackChunks ? n_chunks : kPackChunks;
-        stage(S.pack, d.packed, p0, (int)((pofs + 8 * staged + 15) & ~15u), d.n_elements >> 1, d.async_ok);
+        stage(T.pack, d.packed, p0, (int)((pofs + 8 * staged + 15) & ~15u), d.n_elements >> 1, d.async_ok, t);
         cp_async_commit();
-        int sn = si;
-        if (w + 1 < hi) {
-            sn = find_stream(B.s, si, w + 1);
-            const long long gn = w + 1 - B.s[sn].group_begin;
-            stage_window_bytes(S, buf ^ 1, B.s[sn], gn);
-            r = group_range(B.s[sn], gn);
+        if (g + kTeams < g_end) {
+            stage_window_bytes(T, buf ^ 1, d, g + kTeams, t);
+            r = group_range(d, g + kTeams);
         }
         cp_async_commit();
-        for (int i = t; i < (n_chunks + 1) >> 1; i += kThreads)  // obuf is 16-byte aligned, 4 words a store
-            reinterpret_cast<uint4*>(S.obuf)[i] = make_uint4(0, 0, 0, 0);
+        for (int i = t; i < (n_chunks + 1) >> 1; i += kTeamThreads)  // obuf is 16-byte aligned, 4 words a store
+            reinterpret_cast<uint4*>(T.obuf)[i] = make_uint4(0, 0, 0, 0);
 
         // --- decode this thread's window pair ---
-        uint32_t* slot = S.slot + t * kSlotWords;
         uint32_t count = 0;
         if (g * kGroupBytes + 16 * t < d.n_bytes) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(S.enc[buf] + 16 * t);
-            const uint32_t r4 = *reinterpret_cast<const uint32_t*>(S.enc[buf] + 16 * t + 16);
-            count = decode_run(S, (uint32_t)__cvta_generic_to_shared(slot), __byte_perm(raw.x, 0, 0x0123),
-                               __byte_perm(raw.y, 0, 0x0123),
+            const uint4 raw = *reinterpret_cast<const uint4*>(T.enc[buf] + 16 * t);
+            const uint32_t r4 = *reinterpret_cast<const uint32_t*>(T.enc[buf] + 16 * t + 16);
+            count = decode_run(S, slot_s, __byte_perm(raw.x, 0, 0x0123), __byte_perm(raw.y, 0, 0x0123),
                                __byte_perm(raw.z, 0, 0x0123), __byte_perm(raw.w, 0, 0x0123),
-                               __byte_perm(r4, 0, 0x0123), S.gaps[buf][t] >> 4);
+                               __byte_perm(r4, 0, 0x0123), T.gaps[buf][t] >> 4);
         }
         // A pair wholly past n_bytes only follows the last real code: it places nothing.
 
@@ -475,11 +494,11 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
             const uint32_t y = __shfl_up_sync(0xffffffffu, v, o);
             if (lane >= o) v += y;
         }
-        if (lane == 31) S.wsum[warp] = v;
-        __syncthreads();
-        uint32_t ws = lane < kThreads / 32 ? S.wsum[lane] : 0u;
+        if (lane == 31) T.wsum[warp] = v;
+        team_sync(team);
+        uint32_t ws = lane < kTeamThreads / 32 ? T.wsum[lane] : 0u;
 #pragma unroll
-        for (int o = 1; o < kThreads / 32; o <<= 1) {
+        for (int o = 1; o < kTeamThreads / 32; o <<= 1) {
             const uint32_t y = __shfl_up_sync(0xffffffffu, ws, o);
             if (lane >= o) ws += y;
         }
@@ -496,30 +515,30 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
             uint32_t prev = slot[0];
             uint32_t first = __funnelshift_r(prev, 0u, sh);
             if (nw == 0) first &= tail;
-            atomicOr(&S.obuf[w0], first);
+            atomicOr(&T.obuf[w0], first);
             for (uint32_t q = 1; q < nw; ++q) {
                 const uint32_t cur = slot[q];
-                S.obuf[w0 + q] = __funnelshift_r(cur, prev, sh);
+                T.obuf[w0 + q] = __funnelshift_r(cur, prev, sh);
                 prev = cur;
             }
             if (nw) {
                 const uint32_t cur = nw < kSlotWords ? slot[nw] : 0u;
-                atomicOr(&S.obuf[w0 + nw], __funnelshift_r(cur, prev, sh) & tail);
+                atomicOr(&T.obuf[w0 + nw], __funnelshift_r(cur, prev, sh) & tail);
             }
         }
         cp_async_wait<1>();  // this group's packed nibbles
-        __syncthreads();
+        team_sync(team);
 
         // --- merge with sign+mantissa nibbles, 16 elements per store ---
-        const uint8_t* pk = S.pack + pofs;
+        const uint8_t* pk = T.pack + pofs;
         // Chunks wholly inside [start, end) are stored 16 bytes at a time; the
         // group's first and last chunk may be partial (shared with the
         // neighbouring groups) and are written byte by byte by two threads.
         const int c_first = rs ? 1 : 0;
         const int c_end = (int)(re >> 4);  // chunks [c_first, c_end) are full
         if (d.out16) {
-            for (int c = c_first + t; c < c_end; c += kThreads) {
-                const uint2 ew = *reinterpret_cast<const uint2*>(&S.obuf[2 * c]);
+            for (int c = c_first + t; c < c_end; c += kTeamThreads) {
+                const uint2 ew = *reinterpret_cast<const uint2*>(&T.obuf[2 * c]);
                 const uint2 pw = c < kPackChunks ? *reinterpret_cast<const uint2*>(pk + 8 * c)
                                                  : packed8(d, (base >> 1) + 8ull * c);
                 uint4 o;
@@ -539,9 +558,9 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
             } else if (t == 1 && (re & 15) && (int)(re >> 4) >= c_first) {
                 c = (int)(re >> 4);
             }
-            for (; c >= 0 && c < n_chunks; c = d.out16 ? -1 : c + kThreads) {
+            for (; c >= 0 && c < n_chunks; c = d.out16 ? -1 : c + kTeamThreads) {
                 const uint32_t e0 = 16u * c;
-                const uint2 ew = *reinterpret_cast<const uint2*>(&S.obuf[2 * c]);
+                const uint2 ew = *reinterpret_cast<const uint2*>(&T.obuf[2 * c]);
                 const uint2 pw = c < kPackChunks ? *reinterpret_cast<const uint2*>(pk + 8 * c)
                                                  : packed8(d, (base >> 1) + 8ull * c);
                 uint32_t ow[4];
@@ -553,27 +572,48 @@ __global__ void __launch_bounds__(kThreads, 3) decode_kernel(const __grid_consta
                     if (e0 + k >= rs && e0 + k < re) dst[k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
             }
         }
-
-        if (sn != si) {  // next group belongs to another stream
-            si = sn;
-            __syncthreads();  // all decodes of this group are done with the tables
-            setup_stream(S, B.s[si]);
-        }
     }
     cp_async_wait<0>();
 }
 
-// One CTA derives a stream's multi-symbol table and writes it to `table`.
-__global__ void __launch_bounds__(kThreads, 1) build_table_kernel(const uint8_t* luts, int n_luts,
-                                                                   uint32_t* table) {
+template <int MAXS>
+__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ Batch<MAXS> B) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem& S = *reinterpret_cast<Smem*>(smem_raw);
+    const int team = threadIdx.x / kTeamThreads;
+    const int t = threadIdx.x - team * kTeamThreads;
+    const long long total = B.total_groups;
+    const long long lo = (long long)blockIdx.x * total / gridDim.x;
+    const long long hi = (long long)(blockIdx.x + 1) * total / gridDim.x;
+    if (lo >= hi) return;
+
+    // The CTA's range [lo, hi) in per-stream segments: the tables of one
+    // stream at a time, each team taking every third group of the segment.
+    int si = find_stream(B.s, 0, lo);
+    long long w = lo;
+    for (;;) {
+        const DevStream& d = B.s[si];
+        const long long seg_end = min(hi, d.group_begin + d.n_groups);
+        setup_stream(S, d);
+        decode_groups(S, S.team[team], d, w - d.group_begin + team, seg_end - d.group_begin, team, t);
+        if (seg_end >= hi) break;
+        w = seg_end;
+        si = find_stream(B.s, si, w);
+        __syncthreads();  // every team is done with this stream's tables
+    }
+}
+
+// One CTA derives a stream's multi-symbol table and writes it to `table`.
+__global__ void __launch_bounds__(kTeamThreads, 1) build_table_kernel(const uint8_t* luts, int n_luts,
+                                                                       uint32_t* table) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    TableSmem& S = *reinterpret_cast<TableSmem*>(smem_raw);
     DevStream d{};
     d.luts = luts;
     d.n_luts = n_luts;
     load_luts(S, d);
     derive_table(S);
-    for (int i = threadIdx.x; i < kTabSize; i += kThreads) table[i] = S.tab[i];
+    for (int i = threadIdx.x; i < kTabSize; i += (int)blockDim.x) table[i] = S.tab[i].x;
 }
 
 // ---------------------------------------------------------------------------
@@ -611,7 +651,8 @@ int device_info(DeviceInfo* out) {
             err = cudaFuncSetAttribute(decode_kernel<ECF8_MAX_BATCH>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (err == cudaSuccess)
-            err = cudaFuncSetAttribute(build_table_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+            err = cudaFuncSetAttribute(build_table_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sizeof(TableSmem));
         if (err == cudaSuccess)
             err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&info.blocks_per_sm, decode_kernel<1>,
                                                                 kThreads, smem);
@@ -748,8 +789,8 @@ int ecf8_build_table(const uint8_t* luts, int n_luts, uint32_t* table, void* cud
     ecf8::DeviceInfo info;
     int st = ecf8::device_info(&info);
     if (st != ECF8_OK) return st;
-    ecf8::build_table_kernel<<<1, ecf8::kThreads, sizeof(ecf8::Smem), (cudaStream_t)cuda_stream>>>(luts, n_luts,
-                                                                                                  table);
+    ecf8::build_table_kernel<<<1, ecf8::kTeamThreads, sizeof(ecf8::TableSmem), (cudaStream_t)cuda_stream>>>(
+        luts, n_luts, table);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return ecf8::cuda_fail(e);
     return ECF8_OK;
