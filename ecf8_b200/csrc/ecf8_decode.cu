@@ -78,6 +78,7 @@ struct alignas(16) Smem {
     uint8_t lut[kLutRows * 256];             // reference LUT rows 0..n_luts-2, zero padded
     uint8_t lens[256];                       // reference LUT last row: code lengths
     uint32_t chg[kLutRows * 8];              // per row: bit b set if entry b != entry b-1
+    uint16_t ends[kTabSize];                 // per entry: bit j set if a symbol other than the last ends at j
     Team team[kTeams];
 };
 static_assert(offsetof(Smem, team) % 16 == 0 && offsetof(Smem, tab) % 16 == 0, "vector copies");
@@ -296,6 +297,17 @@ __device__ __forceinline__ uint2 expand_entry(uint32_t e) {
     return b ? make_uint2(e, (b << 24) | (e & 31u)) : make_uint2(0u, 0u);
 }
 
+// Symbol end offsets of every entry but its last symbol's (the run-end fixup
+// of decode_run counts the entry's symbols that start before a bit offset).
+__device__ void build_ends(Smem& S) {
+    for (int i = threadIdx.x; i < kTabSize; i += (int)blockDim.x) {
+        const uint2 e = S.tab[i];
+        S.ends[i] = e.x ? (uint16_t)(entry_ends(S, e.x) & ((1u << (e.y >> 24)) - 1u)) : (uint16_t)0;
+    }
+    __syncthreads();
+}
+__device__ void build_ends(TableSmem&) {}
+
 // LUTs plus the table: copied when prepared, derived otherwise (ends with a barrier).
 template <class SM>
 __device__ void setup_stream(SM& S, const DevStream& d) {
@@ -315,6 +327,7 @@ __device__ void setup_stream(SM& S, const DevStream& d) {
         for (int i = threadIdx.x; i < kTabSize; i += (int)blockDim.x) S.tab[i] = expand_entry(S.tab[i].x);
         __syncthreads();
     }
+    build_ends(S);
 }
 
 // ---------------------------------------------------------------------------
@@ -340,8 +353,16 @@ __device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
     asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
 }
 
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+
+// tail_s: shared address of the run's stream bytes 12..19 (bits 96..159).
 __device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, uint32_t w0, uint32_t w1,
-                                               uint32_t w2, uint32_t w3, uint32_t w4, uint32_t gap) {
+                                               uint32_t w2, uint32_t w3, uint32_t w4, uint32_t gap,
+                                               uint32_t tail_s) {
     const uint32_t tab_s = (uint32_t)__cvta_generic_to_shared(S.tab);
     uint32_t h = __funnelshift_l(w1, w0, gap);
     uint32_t m = __funnelshift_l(w2, w1, gap);
@@ -375,16 +396,14 @@ __device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, u
     if (m4) sts32(slot_s + 4 * words, al << (32 - m4));
     uint32_t n = words * 8 + (m4 >> 2);
     // The last step may have taken codes that start at or after the run's
-    // end; they belong to the next run.
+    // end; they belong to the next run.  The step started at bit 128 - room >
+    // 96; its entry's end offsets tell how many codes start before the end.
     const uint32_t room = 128u - ((K >> 24) - (ehi >> 24));
     if (room < (uint32_t)kTabBits) {
-        const uint32_t c = (elo & 31u) >> 2;
-        uint32_t start = 0, keep = 0;
-        for (uint32_t i = 0; i < c; ++i) {
-            keep += start < room;
-            start += code_length(S, (elo >> (28 - 4 * i)) & 15u);
-        }
-        n -= c - keep;
+        const uint32_t b3 = __byte_perm(lds32(tail_s), 0, 0x0123), b4 = __byte_perm(lds32(tail_s + 4), 0, 0x0123);
+        const uint32_t idx = __funnelshift_l(b4, b3, 32u - room) >> (32 - kTabBits);
+        const uint32_t keep = 1u + __popc(S.ends[idx] & ((1u << room) - 1u));
+        n -= ((elo & 31u) >> 2) - keep;
     }
     return n;
 }
@@ -483,7 +502,8 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, long l
             const uint32_t r4 = *reinterpret_cast<const uint32_t*>(T.enc[buf] + 16 * t + 16);
             count = decode_run(S, slot_s, __byte_perm(raw.x, 0, 0x0123), __byte_perm(raw.y, 0, 0x0123),
                                __byte_perm(raw.z, 0, 0x0123), __byte_perm(raw.w, 0, 0x0123),
-                               __byte_perm(r4, 0, 0x0123), T.gaps[buf][t] >> 4);
+                               __byte_perm(r4, 0, 0x0123), T.gaps[buf][t] >> 4,
+                               (uint32_t)__cvta_generic_to_shared(T.enc[buf] + 16 * t + 12));
         }
         // A pair wholly past n_bytes only follows the last real code: it places nothing.
 
