@@ -44,7 +44,7 @@ namespace {
 constexpr int kGroupWindows = ECF8_THREADS_PER_BLOCK;   // windows per group (512)
 constexpr int kWindowBytes = ECF8_BYTES_PER_THREAD;     // bytes per window (8)
 constexpr int kTeamThreads = kGroupWindows / 2;         // team size: two windows per thread
-constexpr int kTeams = 3;                               // teams per CTA
+constexpr int kTeams = 4;                               // teams per CTA
 constexpr int kThreads = kTeamThreads * kTeams;         // CTA size
 constexpr int kGroupBytes = kGroupWindows * kWindowBytes;  // 4096
 constexpr int kTabBits = 12;                            // multi-symbol table width
@@ -52,17 +52,18 @@ constexpr int kTabSize = 1 << kTabBits;
 constexpr int kMaxSymsPerEntry = 5;                     // 5 nibbles fit in bits 31..12
 constexpr int kSlotWords = 17;                          // 136 nibbles >= 128 + 4 overshoot (odd stride)
 constexpr int kMaxGroupElems = kGroupWindows * 64;      // one symbol per bit at most
-constexpr int kObufWords = (kMaxGroupElems + 32) / 8;   // + 15 head pad, round to 16
+constexpr int kWinChunks = 1024;                        // 16-element output chunks per obuf window
+constexpr int kObufWords = kWinChunks * 2;              // one window: 16384 nibbles
 constexpr int kLutRows = ECF8_MAX_LUTS - 1;             // decode rows (row 0 + prefixes)
 constexpr int kEncStage = kGroupBytes + 16;             // group bytes + look-ahead, 16-byte units
 constexpr int kGapStage = kGroupWindows / 2;            // 4 bits per window
-constexpr int kPackChunks = 1024;                       // 16-element chunks whose nibbles are staged
+constexpr int kPackChunks = kWinChunks;                 // 16-element chunks whose nibbles are staged
 constexpr int kPackStage = kPackChunks * 8 + 16;        // the rest of a (rare) longer group: global loads
 
 // One team's buffers.
 struct alignas(16) Team {
     uint32_t slot[kTeamThreads * kSlotWords];  // per-thread decoded nibbles (MSB first)
-    uint32_t obuf[kObufWords];                 // output-ordered exponent nibbles
+    uint32_t obuf[kObufWords];                 // output-ordered exponent nibbles, one window
     uint8_t enc[2][kEncStage];                 // staged bitstream, double buffered
     uint8_t gaps[2][kGapStage];                // staged gaps, double buffered
     uint8_t pack[kPackStage];                  // staged sign+mantissa nibbles
@@ -133,8 +134,18 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 // Copies bytes [lo, lo + size) of `src` (valid below `limit`) to dst[0, size);
 // size is a multiple of 16.  Asynchronous with cp.async when src + lo is
 // 16-byte aligned, else plain byte loads.
+__device__ __forceinline__ void cp_async16_full(uint32_t dst_s, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst_s), "l"(src) : "memory");
+}
+
 __device__ __forceinline__ void stage(uint8_t* dst, const uint8_t* src, long long lo, int size, long long limit,
                                       bool async_ok, int t) {
+    if (async_ok && lo + size <= limit) {  // the whole range exists: plain 16-byte copies
+        const uint32_t d0 = (uint32_t)__cvta_generic_to_shared(dst);
+        const uint8_t* s0 = src + lo;
+        for (int i = t * 16; i < size; i += kTeamThreads * 16) cp_async16_full(d0 + i, s0 + i);
+        return;
+    }
     const long long vl = limit - lo;
     const int valid = vl < 0 ? 0 : (vl > size ? size : (int)vl);  // bytes of the range that exist
     const uint8_t* s = src + lo;
@@ -459,6 +470,100 @@ __device__ __forceinline__ uint2 packed8(const DevStream& d, unsigned long long 
     return make_uint2(b[0] | b[1] << 8 | b[2] << 16 | b[3] << 24, b[4] | b[5] << 8 | b[6] << 16 | b[7] << 24);
 }
 
+// Copies run nibbles [dpos, dpos + n) (output positions relative to the
+// group's base) from the run's slot into the nibble buffer, whose word 0 is
+// output word wlo.  The run's first and last words are shared with the
+// neighbouring runs (atomicOr into the zeroed buffer); the words in between
+// are its own.  With WIN, words outside the buffer's window are skipped (the
+// unsigned window offsets wrap for words before it).  Reading slot[nw] when
+// nw is the slot size stays in shared memory (the next slot or the buffer)
+// and is masked off by `tail`.
+template <bool WIN>
+__device__ __forceinline__ void place_run(uint32_t* obuf, const uint32_t* slot, uint32_t dpos, uint32_t n,
+                                          uint32_t wlo) {
+    const uint32_t e = dpos + n;
+    const uint32_t nw = ((e - 1) >> 3) - (dpos >> 3);  // words after the first
+    const uint32_t sh = (dpos & 7) * 4;
+    const uint32_t tail = 0xffffffffu << (((8u - (e & 7)) * 4) & 31);
+    const uint32_t o0 = (dpos >> 3) - wlo;
+    uint32_t prev = slot[0];
+    if (!WIN || o0 < (uint32_t)kObufWords) atomicOr(obuf + o0, (prev >> sh) & (nw ? 0xffffffffu : tail));
+    uint32_t q = 1;
+    for (; q + 1 < nw; q += 2) {
+        const uint32_t c0 = slot[q], c1 = slot[q + 1];
+        if (!WIN || o0 + q < (uint32_t)kObufWords) obuf[o0 + q] = __funnelshift_r(c0, prev, sh);
+        if (!WIN || o0 + q + 1 < (uint32_t)kObufWords) obuf[o0 + q + 1] = __funnelshift_r(c1, c0, sh);
+        prev = c1;
+    }
+    if (q < nw) {
+        const uint32_t c0 = slot[q];
+        if (!WIN || o0 + q < (uint32_t)kObufWords) obuf[o0 + q] = __funnelshift_r(c0, prev, sh);
+        prev = c0;
+    }
+    if (nw && (!WIN || o0 + nw < (uint32_t)kObufWords))
+        atomicOr(obuf + o0 + nw, __funnelshift_r(slot[nw], prev, sh) & tail);
+}
+
+// Merges and stores output chunks [c_lo, c_hi) of the group (16 elements
+// each, from base); the nibble buffer holds chunk c_lo at word 0.  Chunks
+// wholly inside the group's range [rs, re) are stored 16 bytes at a time;
+// the group's first and last chunk may be partial (shared with the
+// neighbouring groups) and are written byte by byte by two threads.
+__device__ __forceinline__ void merge_chunks(const Team& T, const DevStream& d, const uint8_t* pk,
+                                             unsigned long long base, uint32_t rs, uint32_t re, int c_lo, int c_hi,
+                                             int t) {
+    const int first_full = rs ? 1 : 0;
+    const int c_first = max(first_full, c_lo);
+    const int c_end = min((int)(re >> 4), c_hi);  // chunks [c_first, c_end) are full
+    const uint2* ew2 = reinterpret_cast<const uint2*>(T.obuf);
+    const uint2* pw2 = reinterpret_cast<const uint2*>(pk);
+    if (d.out16) {
+        uint4* ob = reinterpret_cast<uint4*>(d.out + base);
+        if (c_hi <= kPackChunks) {  // every chunk's packed nibbles are staged
+#pragma unroll 4
+            for (int c = c_first + t; c < c_end; c += kTeamThreads) {
+                const uint2 ew = ew2[c - c_lo], pw = pw2[c];
+                uint4 o;
+                merge8(ew.x, pw.x, o.x, o.y);
+                merge8(ew.y, pw.y, o.z, o.w);
+                ob[c] = o;
+            }
+        } else {
+            for (int c = c_first + t; c < c_end; c += kTeamThreads) {
+                const uint2 ew = ew2[c - c_lo];
+                const uint2 pw = c < kPackChunks ? pw2[c] : packed8(d, (base >> 1) + 8ull * c);
+                uint4 o;
+                merge8(ew.x, pw.x, o.x, o.y);
+                merge8(ew.y, pw.y, o.z, o.w);
+                ob[c] = o;
+            }
+        }
+    }
+    // Byte path: partial chunks (threads 0 and 1), and every chunk when the
+    // output is not 16-byte aligned.
+    const int last = (int)(re >> 4);
+    int c = -1;
+    if (!d.out16) {
+        c = c_lo + t;
+    } else if (t == 0 && rs && c_lo == 0) {
+        c = 0;
+    } else if (t == 1 && (re & 15) && last >= first_full && last >= c_lo && last < c_hi) {
+        c = last;
+    }
+    for (; c >= 0 && c < c_hi; c = d.out16 ? -1 : c + kTeamThreads) {
+        const uint32_t e0 = 16u * c;
+        const uint2 ew = ew2[c - c_lo];
+        const uint2 pw = c < kPackChunks ? pw2[c] : packed8(d, (base >> 1) + 8ull * c);
+        uint32_t ow[4];
+        merge8(ew.x, pw.x, ow[0], ow[1]);
+        merge8(ew.y, pw.y, ow[2], ow[3]);
+        uint8_t* dst = d.out + base + e0;
+#pragma unroll
+        for (int k = 0; k < 16; ++k)
+            if (e0 + k >= rs && e0 + k < re) dst[k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
+    }
+}
+
 // One team decodes groups g0, g0 + kTeams, ... below g_end of stream d.  t is
 // the thread's index in the team; the team's barrier is named barrier team+1.
 __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, long long g0, long long g_end, int team,
@@ -492,7 +597,7 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, long l
             r = group_range(d, g + kTeams);
         }
         cp_async_commit();
-        for (int i = t; i < (n_chunks + 1) >> 1; i += kTeamThreads)  // obuf is 16-byte aligned, 4 words a store
+        for (int i = t; i < (min(n_chunks, kWinChunks) + 1) >> 1; i += kTeamThreads)  // 4 words a store
             reinterpret_cast<uint4*>(T.obuf)[i] = make_uint4(0, 0, 0, 0);
 
         // --- decode this thread's window pair ---
@@ -525,71 +630,29 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, long l
         const uint32_t wbase = __shfl_sync(0xffffffffu, ws, (warp + 31) & 31);
         const uint32_t excl = v - count + (warp ? wbase : 0u);
 
-        // --- place this run's nibbles in output order ---
+        // --- place the runs' nibbles in output order, merge, store ---
+        // A group's output goes through the nibble buffer in windows of
+        // kWinChunks chunks; all but highly compressed groups take one.
         const uint32_t dpos = rs + excl;
-        if (count && dpos < re) {
-            const uint32_t n = min(count, re - dpos);
-            const uint32_t w0 = dpos >> 3, nw = ((dpos + n - 1) >> 3) - w0;  // words after the first
-            const uint32_t sh = (dpos & 7) * 4;
-            const uint32_t tail = (dpos + n) & 7 ? 0xffffffffu << (32 - 4 * ((dpos + n) & 7)) : 0xffffffffu;
-            uint32_t prev = slot[0];
-            uint32_t first = __funnelshift_r(prev, 0u, sh);
-            if (nw == 0) first &= tail;
-            atomicOr(&T.obuf[w0], first);
-            for (uint32_t q = 1; q < nw; ++q) {
-                const uint32_t cur = slot[q];
-                T.obuf[w0 + q] = __funnelshift_r(cur, prev, sh);
-                prev = cur;
-            }
-            if (nw) {
-                const uint32_t cur = nw < kSlotWords ? slot[nw] : 0u;
-                atomicOr(&T.obuf[w0 + nw], __funnelshift_r(cur, prev, sh) & tail);
-            }
-        }
-        cp_async_wait<1>();  // this group's packed nibbles
-        team_sync(team);
-
-        // --- merge with sign+mantissa nibbles, 16 elements per store ---
+        const uint32_t n_place = (count && dpos < re) ? min(count, re - dpos) : 0u;
         const uint8_t* pk = T.pack + pofs;
-        // Chunks wholly inside [start, end) are stored 16 bytes at a time; the
-        // group's first and last chunk may be partial (shared with the
-        // neighbouring groups) and are written byte by byte by two threads.
-        const int c_first = rs ? 1 : 0;
-        const int c_end = (int)(re >> 4);  // chunks [c_first, c_end) are full
-        if (d.out16) {
-            for (int c = c_first + t; c < c_end; c += kTeamThreads) {
-                const uint2 ew = *reinterpret_cast<const uint2*>(&T.obuf[2 * c]);
-                const uint2 pw = c < kPackChunks ? *reinterpret_cast<const uint2*>(pk + 8 * c)
-                                                 : packed8(d, (base >> 1) + 8ull * c);
-                uint4 o;
-                merge8(ew.x, pw.x, o.x, o.y);
-                merge8(ew.y, pw.y, o.z, o.w);
-                *reinterpret_cast<uint4*>(d.out + base + 16u * c) = o;
-            }
-        }
-        {
-            // Byte path: partial chunks (threads 0 and 1), and every chunk
-            // when the output is not 16-byte aligned.
-            int c = -1;
-            if (!d.out16) {
-                c = t;
-            } else if (t == 0 && rs) {
-                c = 0;
-            } else if (t == 1 && (re & 15) && (int)(re >> 4) >= c_first) {
-                c = (int)(re >> 4);
-            }
-            for (; c >= 0 && c < n_chunks; c = d.out16 ? -1 : c + kTeamThreads) {
-                const uint32_t e0 = 16u * c;
-                const uint2 ew = *reinterpret_cast<const uint2*>(&T.obuf[2 * c]);
-                const uint2 pw = c < kPackChunks ? *reinterpret_cast<const uint2*>(pk + 8 * c)
-                                                 : packed8(d, (base >> 1) + 8ull * c);
-                uint32_t ow[4];
-                merge8(ew.x, pw.x, ow[0], ow[1]);
-                merge8(ew.y, pw.y, ow[2], ow[3]);
-                uint8_t* dst = d.out + base + e0;
-#pragma unroll
-                for (int k = 0; k < 16; ++k)
-                    if (e0 + k >= rs && e0 + k < re) dst[k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
+        if (n_chunks <= kWinChunks) {
+            if (n_place) place_run<false>(T.obuf, slot, dpos, n_place, 0);
+            cp_async_wait<1>();  // this group's packed nibbles
+            team_sync(team);
+            merge_chunks(T, d, pk, base, rs, re, 0, n_chunks, t);
+        } else {
+            for (int c_lo = 0; c_lo < n_chunks; c_lo += kWinChunks) {
+                if (c_lo) {
+                    team_sync(team);  // the previous window is merged
+                    for (int i = t; i < kObufWords / 4; i += kTeamThreads)
+                        reinterpret_cast<uint4*>(T.obuf)[i] = make_uint4(0, 0, 0, 0);
+                    team_sync(team);
+                }
+                if (n_place) place_run<true>(T.obuf, slot, dpos, n_place, (uint32_t)c_lo * 2);
+                cp_async_wait<1>();
+                team_sync(team);
+                merge_chunks(T, d, pk, base, rs, re, c_lo, min(n_chunks, c_lo + kWinChunks), t);
             }
         }
     }

@@ -101,6 +101,32 @@ def test_random_streams(cuda_device, oracle_mod, seed):
         assert np.array_equal(run_reference_kernel(s, cuda_device), dec)
 
 
+@pytest.mark.parametrize("k,misalign", [(1, False), (2, False), (2, True), (3, False)])
+def test_highly_compressible_groups(cuda_device, oracle_mod, k, misalign):
+    """Streams of one to three symbols: codes of about one bit put up to
+    32768 elements in a 4096-byte group, more than one pass of the kernel's
+    16384-element output window."""
+    rng = np.random.default_rng(50 + k)
+    s = random_stream(oracle_mod, rng, n=300000, k=k, alpha=0.05)
+    per = np.diff(np.append(s["output_positions"].astype(np.int64), s["fp8"].size))
+    assert per.max() > 16384  # the multi-window path runs
+    dec, guard = decode_guarded(to_device(s, cuda_device), s["fp8"].size, cuda_device, misalign=misalign)
+    assert np.all(guard == GUARD)
+    assert np.array_equal(dec, s["fp8"])
+
+
+def test_highly_compressible_groups_with_prepared_table(cuda_device, oracle_mod):
+    from ecf8_b200.run import build_decode_table, decode_stream
+    rng = np.random.default_rng(61)
+    s = random_stream(oracle_mod, rng, n=300000, k=2, alpha=0.05)
+    d = to_device(s, cuda_device)
+    out = torch.zeros(s["fp8"].size, dtype=torch.uint8, device=cuda_device)
+    decode_stream(d["luts"], d["encoded"], d["packed_other_4bits"], d["output_positions"], d["gaps"], out,
+                  table=build_decode_table(d["luts"]))
+    torch.cuda.synchronize()
+    assert np.array_equal(out.cpu().numpy(), s["fp8"])
+
+
 def test_batch_of_all_golden_streams(cuda_device):
     from ecf8_b200.run import decode_streams
     names = golden_names()
