@@ -384,7 +384,7 @@ def run_ours(args, rank, world, dev):
             "traffic": traffic,
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
             else "fallback 6.65 TB/s",
-            "kernel": "decode_kernel<1>" if world == 1 else "decode_kernel<128>",
+            "kernel": "decode_kernel<128> (ecf8_decode_batch launch)",
             "algorithmic_bytes_per_launch": int(per_launch_bytes),
             "mean_launch_us": round(mean_launch_ms * 1e3, 2),
         },

@@ -48,12 +48,12 @@ def build(verbose=False, extra_flags=()):
         "-Xcompiler", "-fPIC,-O3", "-shared", "-cudart", "shared",
         "-I", os.path.join(ROOT, "include"),
         "-Xlinker", "-rpath," + cuda_lib_dir(),
-        *extra_flags, *srcs, "-o", out + ".tmp",
+        *extra_flags, *srcs, "-o", out + f".tmp{os.getpid()}",
     ]
     if verbose:
         print(" ".join(cmd), file=sys.stderr)
     subprocess.run(cmd, check=True)
-    os.replace(out + ".tmp", out)
+    os.replace(out + f".tmp{os.getpid()}", out)  # per-process temp: ranks may build at once
     return out
 
 
