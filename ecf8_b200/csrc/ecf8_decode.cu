@@ -317,7 +317,6 @@ __device__ void build_ends(Smem& S) {
     }
     __syncthreads();
 }
-__device__ void build_ends(TableSmem&) {}
 
 // LUTs plus the table: copied when prepared, derived otherwise (ends with a barrier).
 template <class SM>
@@ -564,19 +563,73 @@ __device__ __forceinline__ void merge_chunks(const Team& T, const DevStream& d, 
     }
 }
 
+// Merge fast path: one window, 16-byte aligned output, every packed word
+// staged.  Full chunks go out 16 bytes at a time; threads 0 and 1 write the
+// group's partial first and last chunk byte by byte.
+__device__ __forceinline__ void merge_fast(const Team& T, uint8_t* outb, const uint8_t* pk, uint32_t rs,
+                                           uint32_t re, int t) {
+    const int c_first = rs ? 1 : 0;
+    const int c_end = (int)(re >> 4);  // chunks [c_first, c_end) are full
+    const uint2* ew2 = reinterpret_cast<const uint2*>(T.obuf);
+    const uint2* pw2 = reinterpret_cast<const uint2*>(pk);
+    uint4* ob = reinterpret_cast<uint4*>(outb);
+    for (int c = c_first + t; c < c_end; c += kTeamThreads) {
+        const uint2 ew = ew2[c], pw = pw2[c];
+        uint4 o;
+        merge8(ew.x, pw.x, o.x, o.y);
+        merge8(ew.y, pw.y, o.z, o.w);
+        ob[c] = o;
+    }
+    if (t < 2) {
+        const int c = t == 0 ? (rs ? 0 : -1) : ((re & 15) && c_end >= c_first ? c_end : -1);
+        if (c >= 0) {
+            const uint2 ew = ew2[c], pw = pw2[c];
+            uint32_t ow[4];
+            merge8(ew.x, pw.x, ow[0], ow[1]);
+            merge8(ew.y, pw.y, ow[2], ow[3]);
+            const uint32_t e0 = 16u * c;
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+                if (e0 + k >= rs && e0 + k < re) outb[e0 + k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
+        }
+    }
+}
+
 // One team decodes groups g0, g0 + kTeams, ... below g_end of stream d.  t is
 // the thread's index in the team; the team's barrier is named barrier team+1.
-__device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, long long g0, long long g_end, int team,
-                              int t) {
+// Interior groups (whole staging window inside the stream, 16-byte aligned
+// buffers, at most kPackChunks chunks) take straight-line staging and the
+// fast merge; the stream's last groups and unaligned streams take the
+// general paths.
+__device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, int g0, int g_end, int team, int t) {
     if (g0 >= g_end) return;
     const int lane = t & 31, warp = t >> 5;
     uint32_t* slot = T.slot + t * kSlotWords;
     const uint32_t slot_s = (uint32_t)__cvta_generic_to_shared(slot);
-    stage_window_bytes(T, 0, d, g0, t);
+    const long long n_bytes = d.n_bytes;
+    const unsigned long long half = (unsigned long long)d.n_elements >> 1;  // packed bytes
+    // Groups below g_fast have their whole 4112-byte staging window inside the stream.
+    const int g_fast = (d.async_ok && n_bytes >= kEncStage) ? (int)((n_bytes - kEncStage) / kGroupBytes) + 1 : 0;
+    const uint32_t enc_s0 = (uint32_t)__cvta_generic_to_shared(T.enc[0]);
+    const uint32_t gaps_s0 = (uint32_t)__cvta_generic_to_shared(T.gaps[0]);
+    const uint32_t pack_s = (uint32_t)__cvta_generic_to_shared(T.pack);
+    auto stage_windows = [&](int buf, int g) {
+        if (g < g_fast) {
+            const uint8_t* es = d.encoded + (long long)g * kGroupBytes;
+            const uint8_t* gs = d.gaps + (long long)g * kGapStage;
+            const uint32_t eb = enc_s0 + buf * kEncStage, gb = gaps_s0 + buf * kGapStage;
+            cp_async16_full(eb + 16 * t, es + 16 * t);
+            if (t == 0) cp_async16_full(eb + kGroupBytes, es + kGroupBytes);
+            if (t < kGapStage / 16) cp_async16_full(gb + 16 * t, gs + 16 * t);
+        } else {
+            stage_window_bytes(T, buf, d, g, t);
+        }
+    };
+    stage_windows(0, g0);
     cp_async_commit();
     GroupRange r = group_range(d, g0);
     int buf = 0;
-    for (long long g = g0; g < g_end; g += kTeams, buf ^= 1) {
+    for (int g = g0; g < g_end; g += kTeams, buf ^= 1) {
         const unsigned long long start = r.start, end = r.end;
         const unsigned long long base = start & ~15ull;
         const uint32_t rs = (uint32_t)(start - base), re = (uint32_t)(end - base);  // range rel. to base
@@ -587,13 +640,24 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, long l
 
         // Stage this group's packed nibbles and the next group's window bytes;
         // fetch the next group's output range.
-        const long long p0 = (long long)(base >> 1) & ~15ll;
+        const unsigned long long p0 = (base >> 1) & ~15ull;
         const uint32_t pofs = (uint32_t)((base >> 1) - p0);  // 0 or 8
         const int staged = n_chunks < kPackChunks ? n_chunks : kPackChunks;
-        stage(T.pack, d.packed, p0, (int)((pofs + 8 * staged + 15) & ~15u), d.n_elements >> 1, d.async_ok, t);
+        const int pack_bytes = (int)((pofs + 8 * staged + 15) & ~15u);
+        const bool pack_fast = d.async_ok && p0 + pack_bytes <= half;
+        if (pack_fast) {
+            const uint8_t* ps = d.packed + p0;
+            const int units = pack_bytes >> 4;  // <= 513
+            if (t < units) cp_async16_full(pack_s + 16 * t, ps + 16 * t);
+            if (t + kTeamThreads < units) cp_async16_full(pack_s + 16 * (t + kTeamThreads), ps + 16 * (t + kTeamThreads));
+            if (t + 2 * kTeamThreads < units)
+                cp_async16_full(pack_s + 16 * (t + 2 * kTeamThreads), ps + 16 * (t + 2 * kTeamThreads));
+        } else {
+            stage(T.pack, d.packed, (long long)p0, pack_bytes, (long long)half, d.async_ok, t);
+        }
         cp_async_commit();
         if (g + kTeams < g_end) {
-            stage_window_bytes(T, buf ^ 1, d, g + kTeams, t);
+            stage_windows(buf ^ 1, g + kTeams);
             r = group_range(d, g + kTeams);
         }
         cp_async_commit();
@@ -602,13 +666,14 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, long l
 
         // --- decode this thread's window pair ---
         uint32_t count = 0;
-        if (g * kGroupBytes + 16 * t < d.n_bytes) {
+        const long long rem = n_bytes - (long long)g * kGroupBytes;  // stream bytes from this group on
+        if (rem > 16 * t) {
             const uint4 raw = *reinterpret_cast<const uint4*>(T.enc[buf] + 16 * t);
             const uint32_t r4 = *reinterpret_cast<const uint32_t*>(T.enc[buf] + 16 * t + 16);
             count = decode_run(S, slot_s, __byte_perm(raw.x, 0, 0x0123), __byte_perm(raw.y, 0, 0x0123),
                                __byte_perm(raw.z, 0, 0x0123), __byte_perm(raw.w, 0, 0x0123),
                                __byte_perm(r4, 0, 0x0123), T.gaps[buf][t] >> 4,
-                               (uint32_t)__cvta_generic_to_shared(T.enc[buf] + 16 * t + 12));
+                               enc_s0 + buf * kEncStage + 16 * t + 12);
         }
         // A pair wholly past n_bytes only follows the last real code: it places nothing.
 
@@ -640,7 +705,10 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, long l
             if (n_place) place_run<false>(T.obuf, slot, dpos, n_place, 0);
             cp_async_wait<1>();  // this group's packed nibbles
             team_sync(team);
-            merge_chunks(T, d, pk, base, rs, re, 0, n_chunks, t);
+            if (d.out16)
+                merge_fast(T, d.out + base, pk, rs, re, t);
+            else
+                merge_chunks(T, d, pk, base, rs, re, 0, n_chunks, t);
         } else {
             for (int c_lo = 0; c_lo < n_chunks; c_lo += kWinChunks) {
                 if (c_lo) {
@@ -678,7 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
         const DevStream& d = B.s[si];
         const long long seg_end = min(hi, d.group_begin + d.n_groups);
         setup_stream(S, d);
-        decode_groups(S, S.team[team], d, w - d.group_begin + team, seg_end - d.group_begin, team, t);
+        decode_groups(S, S.team[team], d, (int)(w - d.group_begin) + team, (int)(seg_end - d.group_begin), team, t);
         if (seg_end >= hi) break;
         w = seg_end;
         si = find_stream(B.s, si, w);
