@@ -68,6 +68,7 @@ struct alignas(16) Team {
     uint8_t gaps[2][kGapStage];                // staged gaps, double buffered
     uint8_t pack[kPackStage];                  // staged sign+mantissa nibbles
     uint32_t wsum[kTeamThreads / 32];          // scan: warp totals
+    unsigned long long rng[2][2];              // output range [start, end) of the staged groups
 };
 static_assert(offsetof(Team, obuf) % 16 == 0, "obuf must allow 16-byte stores");
 static_assert(offsetof(Team, enc) % 16 == 0 && kEncStage % 16 == 0, "cp.async targets are 16-byte units");
@@ -418,12 +419,22 @@ __device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, u
     return n;
 }
 
+// Bitwise select: bits of x where m is 1, bits of y where m is 0 (one LOP3).
+__device__ __forceinline__ uint32_t bitsel(uint32_t x, uint32_t y, uint32_t m) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xE4;" : "=r"(r) : "r"(x), "r"(y), "r"(m));
+    return r;
+}
+
 // Eight merged e4m3 bytes from eight exponent nibbles (MSB first in `ew`) and
 // four packed sign+mantissa bytes (decode.cu:174-175: out = e<<3 | s<<7 | m).
+// Each output byte takes bit 7 (sign), bits 6..3 (exponent) and bits 2..0
+// (mantissa) from three shifted sources, so two selects build it; the masks
+// cover every bit, so no source needs masking first.
 __device__ __forceinline__ void merge8(uint32_t ew, uint32_t pw, uint32_t& lo, uint32_t& hi) {
     const uint32_t q = __byte_perm(ew, 0, 0x0123);  // byte j = e[2j]<<4 | e[2j+1], like pw
-    const uint32_t ev = (pw & 0x80808080u) | ((q >> 1) & 0x78787878u) | ((pw >> 4) & 0x07070707u);
-    const uint32_t od = ((pw << 4) & 0x80808080u) | ((q << 3) & 0x78787878u) | (pw & 0x07070707u);
+    const uint32_t ev = bitsel(pw, bitsel(pw >> 4, q >> 1, 0x07070707u), 0x80808080u);  // elements 2j
+    const uint32_t od = bitsel(pw << 4, bitsel(pw, q << 3, 0x07070707u), 0x80808080u);  // elements 2j+1
     lo = __byte_perm(ev, od, 0x5140);
     hi = __byte_perm(ev, od, 0x7362);
 }
@@ -627,16 +638,19 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, int g0
     };
     stage_windows(0, g0);
     cp_async_commit();
-    GroupRange r = group_range(d, g0);
+    if (t == 0) {  // thread 0 reads each group's output range one group ahead
+        const GroupRange r0 = group_range(d, g0);
+        T.rng[0][0] = r0.start;
+        T.rng[0][1] = r0.end;
+    }
     int buf = 0;
     for (int g = g0; g < g_end; g += kTeams, buf ^= 1) {
-        const unsigned long long start = r.start, end = r.end;
+        cp_async_wait<0>();  // this group's window bytes
+        team_sync(team);     // ... and its range visible; previous group's merge done with pack / obuf / slots
+        const unsigned long long start = T.rng[buf][0], end = T.rng[buf][1];
         const unsigned long long base = start & ~15ull;
         const uint32_t rs = (uint32_t)(start - base), re = (uint32_t)(end - base);  // range rel. to base
         const int n_chunks = (int)((re + 15) >> 4);
-
-        cp_async_wait<0>();  // this group's window bytes
-        team_sync(team);     // ... visible; previous group's merge done with pack / obuf / slots
 
         // Stage this group's packed nibbles and the next group's window bytes;
         // fetch the next group's output range.
@@ -656,9 +670,10 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, int g0
             stage(T.pack, d.packed, (long long)p0, pack_bytes, (long long)half, d.async_ok, t);
         }
         cp_async_commit();
+        GroupRange rn{0, 0};
         if (g + kTeams < g_end) {
             stage_windows(buf ^ 1, g + kTeams);
-            r = group_range(d, g + kTeams);
+            if (t == 0) rn = group_range(d, g + kTeams);  // stored at the end of the group
         }
         cp_async_commit();
         for (int i = t; i < (min(n_chunks, kWinChunks) + 1) >> 1; i += kTeamThreads)  // 4 words a store
@@ -722,6 +737,10 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, int g0
                 team_sync(team);
                 merge_chunks(T, d, pk, base, rs, re, c_lo, min(n_chunks, c_lo + kWinChunks), t);
             }
+        }
+        if (t == 0 && g + kTeams < g_end) {  // visible after the next group's first barrier
+            T.rng[buf ^ 1][0] = rn.start;
+            T.rng[buf ^ 1][1] = rn.end;
         }
     }
     cp_async_wait<0>();
