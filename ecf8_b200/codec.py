@@ -10,6 +10,8 @@ unchanged:
   get_nbit_codec                         utils.py:239-267
   get_luts_from_huffman_table            utils.py:270-370
   encode_exponents_for_cuda              utils.py:502-530 (packer 373-499)
+  repo_id_to_model_id, locate_block_by_regex, find_layers_by_*
+                                         utils.py:70-185
 
 The LUT layout and the stream layout are the format contract and are
 reproduced exactly.  The code table is this package's own: a Huffman code
@@ -28,6 +30,7 @@ byte-identical to the reference packer for the same code table.
 import ctypes
 import heapq
 import math
+import re
 
 import numpy as np
 import torch
@@ -138,6 +141,79 @@ def flatten_block_of_weights(layers, dtype=torch.float8_e4m3fn):
         off += n
     split_positions = torch.cumsum(torch.tensor(sizes, dtype=torch.int64), 0)[:-1]
     return flat, split_positions
+
+
+def repo_id_to_model_id(repo_id):
+    """'org/name' -> 'models--org--name' (dfloat/utils.py:70-72)."""
+    return "models--" + "--".join(repo_id.split("/"))
+
+
+def locate_block_by_regex(model, pattern):
+    """{full name: module} of every module whose name fully matches `pattern`
+    (dfloat/utils.py:75-80)."""
+    return {n: m for n, m in model.named_modules() if re.fullmatch(pattern, n)}
+
+
+def _child_name(name, child):
+    return f"{name}.{child}" if name else child
+
+
+def find_layers_by_selection(module, select, name=""):
+    """{full name: module} of the sub-modules at the dotted paths in `select`,
+    looked up from `module` and from every module below it, sorted by name
+    (dfloat/utils.py:83-117)."""
+    res = {}
+    for path in select:
+        target = module
+        try:
+            for part in path.split("."):
+                target = getattr(target, part)
+        except AttributeError:
+            continue
+        res[_child_name(name, path)] = target
+    for child_name, child in module.named_children():
+        res.update(find_layers_by_selection(child, select, _child_name(name, child_name)))
+    return dict(sorted(res.items()))
+
+
+def find_layers_by_layer_type(module, layers=(torch.nn.Linear,), name=""):
+    """The outermost modules whose exact type is in `layers`
+    (dfloat/utils.py:120-132)."""
+    if type(module) in tuple(layers):
+        return {name: module}
+    res = {}
+    for child_name, child in module.named_children():
+        res.update(find_layers_by_layer_type(child, layers, _child_name(name, child_name)))
+    return dict(sorted(res.items()))
+
+
+def _weight_dtype(module):
+    w = getattr(module, "weight", None)
+    return getattr(w, "dtype", None)
+
+
+def find_layers_by_data_type(module, target_dtype=torch.bfloat16, name=""):
+    """The outermost modules whose `weight` has `target_dtype`
+    (dfloat/utils.py:135-155)."""
+    if _weight_dtype(module) == target_dtype:
+        return {name: module}
+    res = {}
+    for child_name, child in module.named_children():
+        res.update(find_layers_by_data_type(child, target_dtype, _child_name(name, child_name)))
+    return dict(sorted(res.items()))
+
+
+def find_layers_by_data_type_and_layer_type(module, target_dtype=torch.bfloat16,
+                                            layers=(torch.nn.Linear, torch.nn.Embedding), name=""):
+    """The outermost modules of a type in `layers` whose `weight` has
+    `target_dtype` (dfloat/utils.py:158-185)."""
+    if type(module) in tuple(layers) and _weight_dtype(module) == target_dtype:
+        return {name: module}
+    res = {}
+    for child_name, child in module.named_children():
+        res.update(find_layers_by_data_type_and_layer_type(child, target_dtype, layers,
+                                                           _child_name(name, child_name)))
+    return dict(sorted(res.items()))
 
 
 def get_exponents_and_other_4bits_fp8_e4m3(data):

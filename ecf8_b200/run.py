@@ -437,6 +437,36 @@ def _no_split_classes(model, patterns):
     return out
 
 
+def _is_fp8_config(path):
+    try:
+        with open(os.path.join(path, "config.json")) as f:
+            q = json.load(f).get("quantization_config") or {}
+    except OSError:
+        return False
+    return q.get("quant_method") == "fp8"
+
+
+def _load_original_model(dfloat_repo_id, model_name_or_path, trust_remote_code=True, **kwargs):
+    """The model the compressed blocks go into.  An FP8 checkpoint (config.json
+    with an fp8 quantization_config) is assembled by ecf8_b200.fp8_model, since
+    transformers needs accelerate and hub kernels for it: from the original
+    directory when it is on disk, else from the compressed checkpoint's own
+    config (its safetensors then supply every tensor).  Other models load
+    through transformers as in run.py:483-500."""
+    from .fp8_model import fp8_model_from_config, load_fp8_checkpoint
+    dtype = kwargs.get("torch_dtype", kwargs.get("dtype", torch.bfloat16))
+    if os.path.isdir(model_name_or_path) and _is_fp8_config(model_name_or_path):
+        return load_fp8_checkpoint(model_name_or_path, device="cpu", dtype=dtype)
+    if _is_fp8_config(dfloat_repo_id):
+        from transformers import AutoConfig
+        return fp8_model_from_config(AutoConfig.from_pretrained(dfloat_repo_id), device="cpu", seed=None,
+                                     dtype=dtype)
+    from transformers import AutoModelForCausalLM
+    return AutoModelForCausalLM.from_pretrained(
+        model_name_or_path, trust_remote_code=trust_remote_code, dtype=dtype,
+        attn_implementation=kwargs.get("attn_implementation"), low_cpu_mem_usage=True)
+
+
 class DFloatModel:
     @classmethod
     def from_pretrained(cls, dfloat_repo_id: str, dfloat_model_id: str, model_name_or_path: str,
@@ -450,11 +480,8 @@ class DFloatModel:
         if not os.path.exists(dfloat_repo_id):
             raise FileNotFoundError(
                 f"{dfloat_repo_id} not found (download of {dfloat_model_id} is not available here)")
-        from transformers import AutoConfig, AutoModelForCausalLM
-        model = AutoModelForCausalLM.from_pretrained(
-            model_name_or_path, trust_remote_code=trust_remote_code,
-            torch_dtype=kwargs.get("torch_dtype", torch.bfloat16),
-            attn_implementation=kwargs.get("attn_implementation"), low_cpu_mem_usage=True)
+        from transformers import AutoConfig
+        model = _load_original_model(dfloat_repo_id, model_name_or_path, trust_remote_code, **kwargs)
         model.eval()
         config = AutoConfig.from_pretrained(dfloat_repo_id)
         assert hasattr(config, "dfloat_config")
