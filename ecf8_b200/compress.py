@@ -285,3 +285,29 @@ def main(argv=None):
 
 if __name__ == "__main__":
     main()
+
+
+def compress_model_in_place(model, threads_per_block=512, bytes_per_thread=8, device=None):
+    """Compresses every FP8 block of a model already on the GPU and wires the
+    decode-before-forward hook, without touching disk: the state a model has
+    after compress + DFloatModel.from_pretrained.  Returns the pattern dict."""
+    from .run import _process_compressed_tensor
+    device = device or next(model.parameters()).device
+    pattern = get_fp8_pattern_dict(model.__class__.__name__)
+    blocks = find_fp8_blocks(model, pattern["fp8"])
+    fp8_regex_dict = {}
+    for block_name, layers in sorted(blocks.items()):
+        names = [n[len(block_name) + 1:] for n in layers]
+        regex = next(r for r in pattern["fp8"] if re.fullmatch(r, block_name))
+        fp8_regex_dict.setdefault(regex, names)
+        flat, split_positions = flatten_block_of_weights(layers, dtype=torch.float8_e4m3fn)
+        c = compress_fp8(flat.to(device), device=device)
+        del flat
+        tensors = {"luts": c["luts"], "encoded": c["encoded"], "packed_other_4bits": c["packed_other_4bits"],
+                   "output_positions": c["output_positions"].view(torch.uint8), "gaps": c["gaps"],
+                   "split_positions": split_positions}
+        module = operator.attrgetter(block_name)(model)
+        for key in ("luts", "packed_other_4bits", "output_positions", "gaps", "split_positions", "encoded"):
+            _process_compressed_tensor(module, key, tensors[key], f"{block_name}.{key}", {regex: names},
+                                       threads_per_block, bytes_per_thread)
+    return {"fp8": fp8_regex_dict, "bf16": {r: [] for r in pattern["bf16"]}}

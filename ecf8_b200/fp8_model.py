@@ -41,8 +41,11 @@ class Fp8Linear(nn.Module):
         self.bias = nn.Parameter(torch.zeros(out_features, device=device), requires_grad=False) if bias else None
 
     def dequantized(self, dtype=torch.bfloat16):
-        s = self.weight_scale_inv.repeat_interleave(BLOCK, 0)[: self.out_features]
-        s = s.repeat_interleave(BLOCK, 1)[:, : self.in_features]
+        o, i = self.out_features, self.in_features
+        if o % BLOCK == 0 and i % BLOCK == 0:  # one broadcast multiply per 128x128 tile
+            w = self.weight.view(o // BLOCK, BLOCK, i // BLOCK, BLOCK).to(dtype)
+            return (w * self.weight_scale_inv.to(dtype)[:, None, :, None]).view(o, i)
+        s = self.weight_scale_inv.repeat_interleave(BLOCK, 0)[:o].repeat_interleave(BLOCK, 1)[:, :i]
         return (self.weight.float() * s).to(dtype)
 
     def forward(self, x):
