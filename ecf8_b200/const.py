@@ -46,7 +46,8 @@ MODEL_CLASS_MAP = {
     "llm": {"Qwen3ForCausalLM", "LlamaForCausalLM"},
     "deepseekv3": {"DeepseekV3ForCausalLM"},
     "qwen3moe": {"Qwen3MoeForCausalLM"},
-    "diffsynth-flux-fp8": {"FluxImagePipeline"},
+    # FluxDiTPipeline: the FLUX-shaped DiT of ecf8_b200.dit_model (same block names)
+    "diffsynth-flux-fp8": {"FluxImagePipeline", "FluxDiTPipeline"},
 }
 
 DEFAULT_NO_SPLIT_PATTERN = {

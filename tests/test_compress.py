@@ -67,3 +67,17 @@ def test_compress_cli_rejects_missing_checkpoint(tmp_path):
     from ecf8_b200.compress import main
     with pytest.raises(SystemExit):
         main(["--repo_id", str(tmp_path / "nope")])
+
+
+def test_flux_dit_streams_match_reference_pattern_sizes():
+    """dit.blocks.N / dit.single_blocks.N streams of the FLUX pattern
+    (const.py:30-44): 226,492,416 and 141,557,760 e4m3 weights."""
+    from ecf8_b200.compress import find_fp8_blocks
+    from ecf8_b200.const import get_fp8_pattern_dict
+    from ecf8_b200.dit_model import flux_dit_pipeline
+    p = flux_dit_pipeline(device="cpu", seed=0, n_double=1, n_single=1)
+    blocks = find_fp8_blocks(p, get_fp8_pattern_dict(p.__class__.__name__)["fp8"])
+    sizes = {k: sum(m.weight.numel() for m in v.values()) for k, v in blocks.items()}
+    assert sizes == {"dit.blocks.0": 226492416, "dit.single_blocks.0": 141557760}
+    assert [n[len("dit.single_blocks.0."):] for n in blocks["dit.single_blocks.0"]] == [
+        "norm.linear", "proj_out", "to_qkv_mlp"]
