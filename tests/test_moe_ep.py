@@ -1,0 +1,40 @@
+"""Expert-parallel MoE generation on CPU: two gloo ranks (experts split
+4 + 4, tokens exchanged with all-to-all) generate what one process holding
+all experts generates for both ranks' prompts."""
+import os
+import subprocess
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _single_process_reference(layers, batch, prompt_len, new_tokens, seed=0):
+    from ecf8_b200.moe_ep import MoEConfig, Qwen3MoeEP, greedy_generate, init_random
+    cfg = MoEConfig(vocab_size=256, hidden_size=128, num_hidden_layers=layers, num_attention_heads=4,
+                    num_key_value_heads=2, head_dim=32, num_experts=8, num_experts_per_tok=2,
+                    moe_intermediate_size=128)
+    model = init_random(Qwen3MoeEP(cfg, 0, 1, torch.device("cpu")), seed).eval()
+    ids = []
+    for r in range(2):
+        g = torch.Generator(device="cpu").manual_seed(seed * 7919 + r)
+        ids.append(torch.randint(0, cfg.vocab_size, (batch, prompt_len), generator=g))
+    sums = []
+    tokens = greedy_generate(model, torch.cat(ids), new_tokens, sums)
+    return tokens[:batch], torch.stack(sums)[:, :batch]
+
+
+def test_two_rank_expert_parallel_matches_one_process(tmp_path):
+    out = tmp_path / "ep2.pt"
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", "29561", "-m", "ecf8_b200.inference_moe",
+           "--cpu", "--small", "--layers", "2", "--batch", "2", "--prompt_len", "8", "--new_tokens", "4",
+           "--out", str(out)]
+    env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    r = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-3000:]
+    got = torch.load(out)
+    tokens, sums = _single_process_reference(2, 2, 8, 4)
+    assert torch.equal(got["tokens"], tokens)
+    torch.testing.assert_close(got["logit_sums"], sums, rtol=1e-3, atol=1e-3)
