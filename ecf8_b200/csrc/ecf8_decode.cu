@@ -57,8 +57,6 @@ constexpr int kObufWords = kWinChunks * 2;              // one window: 16384 nib
 constexpr int kLutRows = ECF8_MAX_LUTS - 1;             // decode rows (row 0 + prefixes)
 constexpr int kEncStage = kGroupBytes + 16;             // group bytes + look-ahead, 16-byte units
 constexpr int kGapStage = kGroupWindows / 2;            // 4 bits per window
-constexpr int kPackChunks = kWinChunks;                 // 16-element chunks whose nibbles are staged
-constexpr int kPackStage = kPackChunks * 8 + 16;        // the rest of a (rare) longer group: global loads
 
 // One team's buffers.
 struct alignas(16) Team {
@@ -66,13 +64,12 @@ struct alignas(16) Team {
     uint32_t obuf[kObufWords];                 // output-ordered exponent nibbles, one window
     uint8_t enc[2][kEncStage];                 // staged bitstream, double buffered
     uint8_t gaps[2][kGapStage];                // staged gaps, double buffered
-    uint8_t pack[kPackStage];                  // staged sign+mantissa nibbles
-    uint32_t wsum[kTeamThreads / 32];          // scan: warp totals
+    uint32_t wsum[2][kTeamThreads / 32];       // scan: warp totals, double buffered
     unsigned long long rng[2][2];              // output range [start, end) of the staged groups
 };
 static_assert(offsetof(Team, obuf) % 16 == 0, "obuf must allow 16-byte stores");
 static_assert(offsetof(Team, enc) % 16 == 0 && kEncStage % 16 == 0, "cp.async targets are 16-byte units");
-static_assert(offsetof(Team, gaps) % 16 == 0 && offsetof(Team, pack) % 16 == 0, "cp.async alignment");
+static_assert(offsetof(Team, gaps) % 16 == 0, "cp.async alignment");
 static_assert(sizeof(Team) % 16 == 0, "teams stay 16-byte aligned");
 
 struct alignas(16) Smem {
@@ -515,42 +512,30 @@ __device__ __forceinline__ void place_run(uint32_t* obuf, const uint32_t* slot, 
 }
 
 // Merges and stores output chunks [c_lo, c_hi) of the group (16 elements
-// each, from base); the nibble buffer holds chunk c_lo at word 0.  Chunks
-// wholly inside the group's range [rs, re) are stored 16 bytes at a time;
-// the group's first and last chunk may be partial (shared with the
-// neighbouring groups) and are written byte by byte by two threads.
-__device__ __forceinline__ void merge_chunks(const Team& T, const DevStream& d, const uint8_t* pk,
-                                             unsigned long long base, uint32_t rs, uint32_t re, int c_lo, int c_hi,
-                                             int t) {
+// each, from base); the nibble buffer holds chunk c_lo at word 0 and every
+// word read is zeroed again for the next group.  Packed nibbles are read from
+// global memory.  Chunks wholly inside the group's range [rs, re) are stored
+// 16 bytes at a time when the output is aligned; the group's first and last
+// chunk may be partial (shared with the neighbouring groups) and are written
+// byte by byte by two threads, as every chunk is for unaligned output.
+__device__ __forceinline__ void merge_chunks(Team& T, const DevStream& d, unsigned long long base, uint32_t rs,
+                                             uint32_t re, int c_lo, int c_hi, int t) {
     const int first_full = rs ? 1 : 0;
     const int c_first = max(first_full, c_lo);
     const int c_end = min((int)(re >> 4), c_hi);  // chunks [c_first, c_end) are full
-    const uint2* ew2 = reinterpret_cast<const uint2*>(T.obuf);
-    const uint2* pw2 = reinterpret_cast<const uint2*>(pk);
+    uint2* ew2 = reinterpret_cast<uint2*>(T.obuf);
     if (d.out16) {
         uint4* ob = reinterpret_cast<uint4*>(d.out + base);
-        if (c_hi <= kPackChunks) {  // every chunk's packed nibbles are staged
-#pragma unroll 4
-            for (int c = c_first + t; c < c_end; c += kTeamThreads) {
-                const uint2 ew = ew2[c - c_lo], pw = pw2[c];
-                uint4 o;
-                merge8(ew.x, pw.x, o.x, o.y);
-                merge8(ew.y, pw.y, o.z, o.w);
-                ob[c] = o;
-            }
-        } else {
-            for (int c = c_first + t; c < c_end; c += kTeamThreads) {
-                const uint2 ew = ew2[c - c_lo];
-                const uint2 pw = c < kPackChunks ? pw2[c] : packed8(d, (base >> 1) + 8ull * c);
-                uint4 o;
-                merge8(ew.x, pw.x, o.x, o.y);
-                merge8(ew.y, pw.y, o.z, o.w);
-                ob[c] = o;
-            }
+        for (int c = c_first + t; c < c_end; c += kTeamThreads) {
+            const uint2 ew = ew2[c - c_lo];
+            ew2[c - c_lo] = make_uint2(0u, 0u);
+            const uint2 pw = packed8(d, (base >> 1) + 8ull * c);
+            uint4 o;
+            merge8(ew.x, pw.x, o.x, o.y);
+            merge8(ew.y, pw.y, o.z, o.w);
+            ob[c] = o;
         }
     }
-    // Byte path: partial chunks (threads 0 and 1), and every chunk when the
-    // output is not 16-byte aligned.
     const int last = (int)(re >> 4);
     int c = -1;
     if (!d.out16) {
@@ -563,7 +548,8 @@ __device__ __forceinline__ void merge_chunks(const Team& T, const DevStream& d, 
     for (; c >= 0 && c < c_hi; c = d.out16 ? -1 : c + kTeamThreads) {
         const uint32_t e0 = 16u * c;
         const uint2 ew = ew2[c - c_lo];
-        const uint2 pw = c < kPackChunks ? pw2[c] : packed8(d, (base >> 1) + 8ull * c);
+        ew2[c - c_lo] = make_uint2(0u, 0u);
+        const uint2 pw = packed8(d, (base >> 1) + 8ull * c);
         uint32_t ow[4];
         merge8(ew.x, pw.x, ow[0], ow[1]);
         merge8(ew.y, pw.y, ow[2], ow[3]);
@@ -574,30 +560,39 @@ __device__ __forceinline__ void merge_chunks(const Team& T, const DevStream& d, 
     }
 }
 
-// Merge fast path: one window, 16-byte aligned output, every packed word
-// staged.  Full chunks go out 16 bytes at a time; threads 0 and 1 write the
-// group's partial first and last chunk byte by byte.
-__device__ __forceinline__ void merge_fast(const Team& T, uint8_t* outb, const uint8_t* pk, uint32_t rs,
-                                           uint32_t re, int t) {
+// Merge fast path: one window, 16-byte aligned output and packed nibbles.
+// The packed words of a thread's full chunks (c_first + t + 256 k, k < 4) were
+// loaded into `pw` at the start of the group; every nibble-buffer word read is
+// zeroed again.  Threads 0 and 1 write the group's partial first and last
+// chunk byte by byte.
+__device__ __forceinline__ void merge_fast(Team& T, const DevStream& d, unsigned long long base, uint32_t rs,
+                                           uint32_t re, int t, const uint2 (&pw)[4]) {
     const int c_first = rs ? 1 : 0;
     const int c_end = (int)(re >> 4);  // chunks [c_first, c_end) are full
-    const uint2* ew2 = reinterpret_cast<const uint2*>(T.obuf);
-    const uint2* pw2 = reinterpret_cast<const uint2*>(pk);
+    uint2* ew2 = reinterpret_cast<uint2*>(T.obuf);
+    uint8_t* outb = d.out + base;
     uint4* ob = reinterpret_cast<uint4*>(outb);
-    for (int c = c_first + t; c < c_end; c += kTeamThreads) {
-        const uint2 ew = ew2[c], pw = pw2[c];
-        uint4 o;
-        merge8(ew.x, pw.x, o.x, o.y);
-        merge8(ew.y, pw.y, o.z, o.w);
-        ob[c] = o;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int c = c_first + t + k * kTeamThreads;
+        if (c < c_end) {
+            const uint2 ew = ew2[c];
+            ew2[c] = make_uint2(0u, 0u);
+            uint4 o;
+            merge8(ew.x, pw[k].x, o.x, o.y);
+            merge8(ew.y, pw[k].y, o.z, o.w);
+            ob[c] = o;
+        }
     }
     if (t < 2) {
         const int c = t == 0 ? (rs ? 0 : -1) : ((re & 15) && c_end >= c_first ? c_end : -1);
         if (c >= 0) {
-            const uint2 ew = ew2[c], pw = pw2[c];
+            const uint2 ew = ew2[c];
+            ew2[c] = make_uint2(0u, 0u);
+            const uint2 p = packed8(d, (base >> 1) + 8ull * c);
             uint32_t ow[4];
-            merge8(ew.x, pw.x, ow[0], ow[1]);
-            merge8(ew.y, pw.y, ow[2], ow[3]);
+            merge8(ew.x, p.x, ow[0], ow[1]);
+            merge8(ew.y, p.y, ow[2], ow[3]);
             const uint32_t e0 = 16u * c;
 #pragma unroll
             for (int k = 0; k < 16; ++k)
@@ -608,8 +603,17 @@ __device__ __forceinline__ void merge_fast(const Team& T, uint8_t* outb, const u
 
 // One team decodes groups g0, g0 + kTeams, ... below g_end of stream d.  t is
 // the thread's index in the team; the team's barrier is named barrier team+1.
-// Interior groups (whole staging window inside the stream, 16-byte aligned
-// buffers, at most kPackChunks chunks) take straight-line staging and the
+//
+// Two barriers per group.  The first (after the decode) publishes the warp
+// totals of the scan, the next group's staged bitstream (each thread waits for
+// its own copies just before it) and the next group's range (read by thread 0
+// one group ahead); the second publishes the nibble buffer for the merge.  No
+// barrier is needed at the top of a group: the staging buffers and warp
+// totals are double buffered, the slots are private, and the merge zeroes
+// every nibble-buffer word it reads, so the buffer is zero again before any
+// thread passes the next group's first barrier.  Interior groups (whole
+// staging window inside the stream, 16-byte aligned buffers, one window) load
+// their packed nibbles into registers at the start of the group and take the
 // fast merge; the stream's last groups and unaligned streams take the
 // general paths.
 __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, int g0, int g_end, int team, int t) {
@@ -618,12 +622,10 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, int g0
     uint32_t* slot = T.slot + t * kSlotWords;
     const uint32_t slot_s = (uint32_t)__cvta_generic_to_shared(slot);
     const long long n_bytes = d.n_bytes;
-    const unsigned long long half = (unsigned long long)d.n_elements >> 1;  // packed bytes
     // Groups below g_fast have their whole 4112-byte staging window inside the stream.
     const int g_fast = (d.async_ok && n_bytes >= kEncStage) ? (int)((n_bytes - kEncStage) / kGroupBytes) + 1 : 0;
     const uint32_t enc_s0 = (uint32_t)__cvta_generic_to_shared(T.enc[0]);
     const uint32_t gaps_s0 = (uint32_t)__cvta_generic_to_shared(T.gaps[0]);
-    const uint32_t pack_s = (uint32_t)__cvta_generic_to_shared(T.pack);
     auto stage_windows = [&](int buf, int g) {
         if (g < g_fast) {
             const uint8_t* es = d.encoded + (long long)g * kGroupBytes;
@@ -636,6 +638,8 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, int g0
             stage_window_bytes(T, buf, d, g, t);
         }
     };
+    for (int i = t; i < kObufWords / 4; i += kTeamThreads)
+        reinterpret_cast<uint4*>(T.obuf)[i] = make_uint4(0, 0, 0, 0);
     stage_windows(0, g0);
     cp_async_commit();
     if (t == 0) {  // thread 0 reads each group's output range one group ahead
@@ -643,41 +647,34 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, int g0
         T.rng[0][0] = r0.start;
         T.rng[0][1] = r0.end;
     }
+    cp_async_wait<0>();
+    team_sync(team);
     int buf = 0;
     for (int g = g0; g < g_end; g += kTeams, buf ^= 1) {
-        cp_async_wait<0>();  // this group's window bytes
-        team_sync(team);     // ... and its range visible; previous group's merge done with pack / obuf / slots
         const unsigned long long start = T.rng[buf][0], end = T.rng[buf][1];
         const unsigned long long base = start & ~15ull;
         const uint32_t rs = (uint32_t)(start - base), re = (uint32_t)(end - base);  // range rel. to base
         const int n_chunks = (int)((re + 15) >> 4);
+        const bool fast = d.out16 && d.async_ok && n_chunks <= kWinChunks;
 
-        // Stage this group's packed nibbles and the next group's window bytes;
-        // fetch the next group's output range.
-        const unsigned long long p0 = (base >> 1) & ~15ull;
-        const uint32_t pofs = (uint32_t)((base >> 1) - p0);  // 0 or 8
-        const int staged = n_chunks < kPackChunks ? n_chunks : kPackChunks;
-        const int pack_bytes = (int)((pofs + 8 * staged + 15) & ~15u);
-        const bool pack_fast = d.async_ok && p0 + pack_bytes <= half;
-        if (pack_fast) {
-            const uint8_t* ps = d.packed + p0;
-            const int units = pack_bytes >> 4;  // <= 513
-            if (t < units) cp_async16_full(pack_s + 16 * t, ps + 16 * t);
-            if (t + kTeamThreads < units) cp_async16_full(pack_s + 16 * (t + kTeamThreads), ps + 16 * (t + kTeamThreads));
-            if (t + 2 * kTeamThreads < units)
-                cp_async16_full(pack_s + 16 * (t + 2 * kTeamThreads), ps + 16 * (t + 2 * kTeamThreads));
-        } else {
-            stage(T.pack, d.packed, (long long)p0, pack_bytes, (long long)half, d.async_ok, t);
-        }
-        cp_async_commit();
+        // Stage the next group's window bytes; read its output range.
         GroupRange rn{0, 0};
         if (g + kTeams < g_end) {
             stage_windows(buf ^ 1, g + kTeams);
-            if (t == 0) rn = group_range(d, g + kTeams);  // stored at the end of the group
+            if (t == 0) rn = group_range(d, g + kTeams);
         }
         cp_async_commit();
-        for (int i = t; i < (min(n_chunks, kWinChunks) + 1) >> 1; i += kTeamThreads)  // 4 words a store
-            reinterpret_cast<uint4*>(T.obuf)[i] = make_uint4(0, 0, 0, 0);
+        // This thread's packed words for the fast merge, in flight during the decode.
+        uint2 pw[4];
+        if (fast) {
+            const int c_first = rs ? 1 : 0, c_end = (int)(re >> 4);
+            const uint2* src = reinterpret_cast<const uint2*>(d.packed + (base >> 1));
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int c = c_first + t + k * kTeamThreads;
+                pw[k] = c < c_end ? __ldg(src + c) : make_uint2(0u, 0u);
+            }
+        }
 
         // --- decode this thread's window pair ---
         uint32_t count = 0;
@@ -699,9 +696,14 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, int g0
             const uint32_t y = __shfl_up_sync(0xffffffffu, v, o);
             if (lane >= o) v += y;
         }
-        if (lane == 31) T.wsum[warp] = v;
+        if (lane == 31) T.wsum[buf][warp] = v;
+        if (t == 0 && g + kTeams < g_end) {
+            T.rng[buf ^ 1][0] = rn.start;
+            T.rng[buf ^ 1][1] = rn.end;
+        }
+        cp_async_wait<0>();  // this thread's copies of the next group's window bytes
         team_sync(team);
-        uint32_t ws = lane < kTeamThreads / 32 ? T.wsum[lane] : 0u;
+        uint32_t ws = lane < kTeamThreads / 32 ? T.wsum[buf][lane] : 0u;
 #pragma unroll
         for (int o = 1; o < kTeamThreads / 32; o <<= 1) {
             const uint32_t y = __shfl_up_sync(0xffffffffu, ws, o);
@@ -715,32 +717,20 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, int g0
         // kWinChunks chunks; all but highly compressed groups take one.
         const uint32_t dpos = rs + excl;
         const uint32_t n_place = (count && dpos < re) ? min(count, re - dpos) : 0u;
-        const uint8_t* pk = T.pack + pofs;
         if (n_chunks <= kWinChunks) {
             if (n_place) place_run<false>(T.obuf, slot, dpos, n_place, 0);
-            cp_async_wait<1>();  // this group's packed nibbles
             team_sync(team);
-            if (d.out16)
-                merge_fast(T, d.out + base, pk, rs, re, t);
+            if (fast)
+                merge_fast(T, d, base, rs, re, t, pw);
             else
-                merge_chunks(T, d, pk, base, rs, re, 0, n_chunks, t);
+                merge_chunks(T, d, base, rs, re, 0, n_chunks, t);
         } else {
             for (int c_lo = 0; c_lo < n_chunks; c_lo += kWinChunks) {
-                if (c_lo) {
-                    team_sync(team);  // the previous window is merged
-                    for (int i = t; i < kObufWords / 4; i += kTeamThreads)
-                        reinterpret_cast<uint4*>(T.obuf)[i] = make_uint4(0, 0, 0, 0);
-                    team_sync(team);
-                }
+                if (c_lo) team_sync(team);  // the previous window is merged (and zeroed)
                 if (n_place) place_run<true>(T.obuf, slot, dpos, n_place, (uint32_t)c_lo * 2);
-                cp_async_wait<1>();
                 team_sync(team);
-                merge_chunks(T, d, pk, base, rs, re, c_lo, min(n_chunks, c_lo + kWinChunks), t);
+                merge_chunks(T, d, base, rs, re, c_lo, min(n_chunks, c_lo + kWinChunks), t);
             }
-        }
-        if (t == 0 && g + kTeams < g_end) {  // visible after the next group's first barrier
-            T.rng[buf ^ 1][0] = rn.start;
-            T.rng[buf ^ 1][1] = rn.end;
         }
     }
     cp_async_wait<0>();
