@@ -18,6 +18,8 @@ ERR_CUDA = 3
 ERR_TOO_LARGE = 4
 NOALLOC_MAX_ELEMENTS = 268435456
 
+ABI_VERSION = 3
+TABLE_BYTES = 81920  # prepared decode table (ecf8_build_table)
 MAX_LUTS = 18
 MAX_BATCH = 128
 THREADS_PER_BLOCK = 512
@@ -93,7 +95,7 @@ def lib():
                 fn = getattr(handle, name)
                 fn.restype = res
                 fn.argtypes = args
-            if handle.ecf8_abi_version() != 2:
+            if handle.ecf8_abi_version() != ABI_VERSION:
                 raise RuntimeError("ECF8 CUDA library ABI version mismatch")
             _lib = handle
     return _lib

@@ -5,13 +5,13 @@
 // like the reference kernel dfloat/run/decode.cu:16-211, with a different
 // design:
 //
-//  * Persistent CTAs of three teams.  One CTA of 768 threads per SM holds
+//  * Persistent CTAs of four teams.  One CTA of 1024 threads per SM holds
 //    one copy of the stream's decode tables in shared memory; each team of
-//    256 threads walks every third 4096-byte group (one reference thread
+//    256 threads walks every fourth 4096-byte group (one reference thread
 //    block's worth of stream) of the CTA's range, synchronising on its own
 //    named barrier, so the teams' phases interleave like separate CTAs.
-//  * Multi-symbol table.  A 4096-entry table indexed by the next 12 stream
-//    bits yields up to five whole symbols, the bits they use and their count,
+//  * Multi-symbol table.  An 8192-entry table indexed by the next 13 stream
+//    bits yields up to six whole symbols, the bits they use and their count,
 //    plus a counter step that advances the bit position, the output nibble
 //    count and the output word address with one add.  It is a pure function
 //    of the stream's LUTs: ecf8_build_table() derives it once per stream (at
@@ -47,9 +47,9 @@ constexpr int kTeamThreads = kGroupWindows / 2;         // team size: two window
 constexpr int kTeams = 4;                               // teams per CTA
 constexpr int kThreads = kTeamThreads * kTeams;         // CTA size
 constexpr int kGroupBytes = kGroupWindows * kWindowBytes;  // 4096
-constexpr int kTabBits = 12;                            // multi-symbol table width
+constexpr int kTabBits = 13;                            // multi-symbol table width
 constexpr int kTabSize = 1 << kTabBits;
-constexpr int kMaxSymsPerEntry = 5;                     // 5 nibbles fit in bits 31..12
+constexpr int kMaxSymsPerEntry = 6;                     // 6 nibbles fit in bits 31..8
 constexpr int kSlotWords = 17;                          // 136 nibbles >= 128 + 4 overshoot (odd stride)
 constexpr int kMaxGroupElems = kGroupWindows * 64;      // one symbol per bit at most
 constexpr int kWinChunks = 1024;                        // 16-element output chunks per obuf window
@@ -80,7 +80,8 @@ struct alignas(16) Smem {
     uint16_t ends[kTabSize];                 // per entry: bit j set if a symbol other than the last ends at j
     Team team[kTeams];
 };
-static_assert(offsetof(Smem, team) % 16 == 0 && offsetof(Smem, tab) % 16 == 0, "vector copies");
+static_assert(offsetof(Smem, team) % 16 == 0 && offsetof(Smem, tab) % 16 == 0 && offsetof(Smem, ends) % 16 == 0,
+              "vector copies");
 
 // Shared-memory layout of build_table_kernel: the decode tables only.
 struct alignas(16) TableSmem {
@@ -99,7 +100,7 @@ struct DevStream {
     const uint64_t* op;
     const uint8_t* gaps;
     uint8_t* out;
-    const uint32_t* table;  // prepared multi-symbol table (4096 entries) or null
+    const uint32_t* table;  // prepared multi-symbol table (8192 64-bit entries) or null
     long long n_bytes;
     long long n_elements;
     long long n_op;
@@ -159,12 +160,12 @@ __device__ __forceinline__ void stage(uint8_t* dst, const uint8_t* src, long lon
 }
 
 // ---------------------------------------------------------------------------
-// Per-stream set-up.  Entry layout (u32): bits 31..12 up to five 4-bit
-// symbols, first symbol in the top nibble; bits 11..8 the number of stream
-// bits the symbols use; bits 4..0 four times the symbol count (so the entry
-// is directly a funnel-shift amount).  An all-zero entry means no complete
-// code starts the pattern within 12 bits; the decoder then uses the
-// two-level LUT directly.
+// Per-stream set-up.  Entry layout (64 bits): x holds up to six 4-bit
+// symbols, first symbol in bits 31..28, and four times the symbol count in
+// bits 4..0 (directly a funnel-shift amount); y is the counter step (bits the
+// symbols use) << 24 | four times the count.  An all-zero entry means no
+// complete code starts the pattern within the 13 bits; the decoder then uses
+// the two-level LUT directly.
 // ---------------------------------------------------------------------------
 template <class SM>
 __device__ __forceinline__ uint32_t lut_symbol(const SM& S, uint32_t top) {
@@ -182,7 +183,7 @@ __device__ __forceinline__ uint32_t code_length(const SM& S, uint32_t sym) {
     return len ? len : 1u;
 }
 
-// Bit j set for the end offset of each symbol of entry e (offsets 1..12).
+// Bit j set for the end offset of each symbol of entry e (offsets 1..13).
 template <class SM>
 __device__ __forceinline__ uint32_t entry_ends(const SM& S, uint32_t e) {
     const uint32_t c = (e & 31u) >> 2;
@@ -248,6 +249,23 @@ __device__ void load_luts(SM& S, const DevStream& d) {
     __syncthreads();
 }
 
+// A table entry (64 bits): x = up to six 4-bit symbols, first in bits 31..28,
+// with 4 x count in bits 4..0; y = the counter step (bits << 24) | 4 x count
+// (see decode_run).  All zero: no complete code within the table width.
+__device__ __forceinline__ uint2 make_entry(uint32_t syms, uint32_t bits, uint32_t count) {
+    return count ? make_uint2(syms | (4 * count), (bits << 24) | (4 * count)) : make_uint2(0u, 0u);
+}
+
+// A prepared entry as read from memory, with every field the decode relies
+// on forced into range (bits 1..kTabBits, count 1..kMaxSymsPerEntry), so a
+// table that ecf8_build_table did not write cannot stall or overrun a run.
+__device__ __forceinline__ uint2 sanitize_entry(uint2 e) {
+    const uint32_t b = e.y >> 24, c4 = e.x & 31u;
+    if (e.x == 0 || b == 0 || b > (uint32_t)kTabBits || c4 == 0 || (c4 & 3u) || c4 > 4u * kMaxSymsPerEntry)
+        return make_uint2(0u, 0u);
+    return make_entry(e.x & 0xffffff00u, b, c4 >> 2);
+}
+
 // Derives the multi-symbol table from the LUTs in shared memory (all threads).
 template <class SM>
 __device__ void derive_table(SM& S) {
@@ -267,19 +285,20 @@ __device__ void derive_table(SM& S) {
             pos += len;
             ++c;
         }
-        S.tab[0].x = syms | (pos << 8) | (4 * c);
+        S.tab[0] = make_entry(syms, pos, c);
     }
     __syncthreads();
-    // Entry x from entry y = (x << l) & 0xfff, where l is x's first code length:
-    // y's codes that end within the remaining 12 - l bits follow.  y has more
-    // trailing zeros than x, so entries are built in order of decreasing
+    // Entry x from entry y = (x << l) mod 2^kTabBits, where l is x's first
+    // code length: y's codes that end within the remaining bits follow.  y has
+    // more trailing zeros than x, so entries are built in order of decreasing
     // trailing-zero count, one round per count.
     for (int tz = kTabBits - 1; tz >= 0; --tz) {
         const int n = 1 << (kTabBits - 1 - tz);
         for (int j = t; j < n; j += (int)blockDim.x) {
             const uint32_t x = (uint32_t)(2 * j + 1) << tz;
-            uint32_t sym, len, ent = 0;
-            if (real_code(S, x << 4, sym, len) && len <= (uint32_t)kTabBits) {
+            uint32_t sym, len;
+            uint2 ent = make_uint2(0u, 0u);
+            if (real_code(S, x << (16 - kTabBits), sym, len) && len <= (uint32_t)kTabBits) {
                 uint32_t kept = 0, endk = 0, rest = 0;
                 if (len < (uint32_t)kTabBits) {
                     const uint32_t ey = S.tab[(x << len) & (kTabSize - 1)].x;
@@ -290,52 +309,45 @@ __device__ void derive_table(SM& S) {
                         rest = (ey >> 4) & (((1u << (4 * kept)) - 1u) << (28 - 4 * kept));
                     }
                 }
-                ent = ((sym & 15u) << 28) | rest | ((len + endk) << 8) | (4 * (1 + kept));
+                ent = make_entry(((sym & 15u) << 28) | rest, len + endk, 1 + kept);
             }
-            S.tab[x].x = ent;
+            S.tab[x] = ent;
         }
         __syncthreads();
     }
 }
 
-// Counter step of a table entry (see decode_run): (bits << 24) | 4 x count.  An
-// entry without a complete code (bits 0) becomes all-zero, which sends the
-// decode to the two-level LUT, whatever the rest of the entry holds.
-__device__ __forceinline__ uint2 expand_entry(uint32_t e) {
-    const uint32_t b = (e >> 8) & 15u;
-    return b ? make_uint2(e, (b << 24) | (e & 31u)) : make_uint2(0u, 0u);
-}
-
 // Symbol end offsets of every entry but its last symbol's (the run-end fixup
 // of decode_run counts the entry's symbols that start before a bit offset).
+template <class SM>
+__device__ __forceinline__ uint16_t entry_start_mask(const SM& S, uint2 e) {
+    return e.x ? (uint16_t)(entry_ends(S, e.x) & ((1u << (e.y >> 24)) - 1u)) : (uint16_t)0;
+}
+
 __device__ void build_ends(Smem& S) {
-    for (int i = threadIdx.x; i < kTabSize; i += (int)blockDim.x) {
-        const uint2 e = S.tab[i];
-        S.ends[i] = e.x ? (uint16_t)(entry_ends(S, e.x) & ((1u << (e.y >> 24)) - 1u)) : (uint16_t)0;
-    }
+    for (int i = threadIdx.x; i < kTabSize; i += (int)blockDim.x) S.ends[i] = entry_start_mask(S, S.tab[i]);
     __syncthreads();
 }
 
 // LUTs plus the table: copied when prepared, derived otherwise (ends with a barrier).
 template <class SM>
 __device__ void setup_stream(SM& S, const DevStream& d) {
-    if (d.table) {
+    if (d.table) {  // entries, then the end masks (any mask value is safe)
         const uint4* src = reinterpret_cast<const uint4*>(d.table);
         uint4* dst = reinterpret_cast<uint4*>(S.tab);
-        for (int i = threadIdx.x; i < kTabSize / 4; i += (int)blockDim.x) {
+        for (int i = threadIdx.x; i < kTabSize / 2; i += (int)blockDim.x) {
             const uint4 q = __ldg(src + i);
-            const uint2 a = expand_entry(q.x), b = expand_entry(q.y), c = expand_entry(q.z), e = expand_entry(q.w);
-            dst[2 * i] = make_uint4(a.x, a.y, b.x, b.y);
-            dst[2 * i + 1] = make_uint4(c.x, c.y, e.x, e.y);
+            const uint2 a = sanitize_entry(make_uint2(q.x, q.y)), b = sanitize_entry(make_uint2(q.z, q.w));
+            dst[i] = make_uint4(a.x, a.y, b.x, b.y);
         }
+        uint4* ends = reinterpret_cast<uint4*>(S.ends);
+        for (int i = threadIdx.x; i < kTabSize / 8; i += (int)blockDim.x) ends[i] = __ldg(src + kTabSize / 2 + i);
         load_luts(S, d);
     } else {
         load_luts(S, d);
         derive_table(S);
-        for (int i = threadIdx.x; i < kTabSize; i += (int)blockDim.x) S.tab[i] = expand_entry(S.tab[i].x);
-        __syncthreads();
+        build_ends(S);
     }
-    build_ends(S);
 }
 
 // ---------------------------------------------------------------------------
@@ -773,7 +785,12 @@ __global__ void __launch_bounds__(kTeamThreads, 1) build_table_kernel(const uint
     d.n_luts = n_luts;
     load_luts(S, d);
     derive_table(S);
-    for (int i = threadIdx.x; i < kTabSize; i += (int)blockDim.x) table[i] = S.tab[i].x;
+    uint2* out = reinterpret_cast<uint2*>(table);
+    uint16_t* ends = reinterpret_cast<uint16_t*>(out + kTabSize);
+    for (int i = threadIdx.x; i < kTabSize; i += (int)blockDim.x) {
+        out[i] = S.tab[i];
+        ends[i] = entry_start_mask(S, S.tab[i]);
+    }
 }
 
 // ---------------------------------------------------------------------------

@@ -88,14 +88,14 @@ def _check_u8(t, name, device):
 
 
 def build_decode_table(luts, stream=None):
-    """The stream's 4096-entry multi-symbol decode table (int32 tensor on the
+    """The stream's multi-symbol decode table (_lib.TABLE_BYTES as an int32 tensor on the
     LUTs' device), derived from its LUTs by ecf8_build_table.  It depends on
     the LUTs only: build it once per stream and pass it to every decode."""
     device = luts.device
     _check_u8(luts, "luts", device)
     if device.type != "cuda":
         raise ValueError("the decode table is built on a CUDA device")
-    table = torch.empty(4096, dtype=torch.int32, device=device)
+    table = torch.empty(_lib.TABLE_BYTES // 4, dtype=torch.int32, device=device)
     with torch.cuda.device(device):
         s = stream if stream is not None else torch.cuda.current_stream(device)
         st = _lib.lib().ecf8_build_table(luts.data_ptr(), luts.shape[0], table.data_ptr(), s.cuda_stream)
@@ -124,8 +124,8 @@ def _check_stream(s, out, device, table=None):
         raise ValueError(f"out holds {out.numel() * out.element_size()} bytes, the stream has {n} elements")
     if table is not None:
         _check_u8(table, "table", device)
-        if table.numel() * table.element_size() != 4096 * 4:
-            raise ValueError("a decode table has 4096 32-bit entries")
+        if table.numel() * table.element_size() != _lib.TABLE_BYTES:
+            raise ValueError(f"a decode table has {_lib.TABLE_BYTES} bytes")
 
 
 def decode_stream(luts, encoded, packed_other_4bits, output_positions, gaps, out=None,

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ECF8_ABI_VERSION 2
+#define ECF8_ABI_VERSION 3
 
 /* Status codes. */
 #define ECF8_OK 0
@@ -46,6 +46,7 @@ extern "C" {
 #define ECF8_THREADS_PER_BLOCK 512 /* windows per group (compress.py:7) */
 #define ECF8_MAX_LUTS 18           /* row 0 + 16 prefix rows + length row */
 #define ECF8_MAX_BATCH 128         /* streams per ecf8_decode_batch launch */
+#define ECF8_TABLE_BYTES 81920     /* prepared decode table (ecf8_build_table) */
 
 /* One stream of a batched decode; field meaning as in ecf8_decode(). */
 typedef struct ecf8_stream {
@@ -61,7 +62,7 @@ typedef struct ecf8_stream {
     int64_t n_gap_bytes;
     uint8_t* outputs;
     int64_t n_elements;
-    const uint32_t* table; /* from ecf8_build_table(), or NULL (derived in-kernel) */
+    const uint32_t* table; /* ECF8_TABLE_BYTES from ecf8_build_table(), or NULL (derived in-kernel) */
 } ecf8_stream;
 
 /*
@@ -91,13 +92,15 @@ int ecf8_decode(const uint8_t* luts, const uint8_t* encoded,
                 int bytes_per_thread, void* cuda_stream);
 
 /*
- * Derives a stream's 4096-entry multi-symbol decode table (16 KB, 16-byte
- * aligned device memory) from its LUTs, asynchronously on cuda_stream.  The
- * table depends on the LUTs only, so it can be built once when a stream is
- * loaded and passed in ecf8_stream.table to every later decode; decodes
- * without it derive the table inside the kernel.  Corresponds to the
- * per-block set-up the reference loader does once
- * (dfloat/run/run.py:453-458, shared_mem_size).
+ * Derives a stream's multi-symbol decode table (ECF8_TABLE_BYTES = 80 KB,
+ * 16-byte aligned device memory: 8192 64-bit entries, one per 13-bit stream
+ * prefix, each up to six whole symbols with their bit and symbol counts,
+ * followed by one 16-bit mask of symbol start offsets per entry) from its
+ * LUTs, asynchronously on cuda_stream.  The table depends on the LUTs
+ * only, so it can be built once when a stream is loaded and passed in
+ * ecf8_stream.table to every later decode; decodes without it derive the
+ * table inside the kernel.  Corresponds to the per-block set-up the reference
+ * loader does once (dfloat/run/run.py:453-458, shared_mem_size).
  */
 int ecf8_build_table(const uint8_t* luts, int n_luts, uint32_t* table,
                      void* cuda_stream);
