@@ -628,8 +628,7 @@ __device__ __forceinline__ void merge_fast(Team& T, const DevStream& d, unsigned
 // their packed nibbles into registers at the start of the group and take the
 // fast merge; the stream's last groups and unaligned streams take the
 // general paths.
-__device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, int g0, int g_end, int team, int t) {
-    if (g0 >= g_end) return;
+__device__ void decode_groups(Smem& S, Team& T, const DevStream& d, int g0, int g_end, int team, int t) {
     const int lane = t & 31, warp = t >> 5;
     uint32_t* slot = T.slot + t * kSlotWords;
     const uint32_t slot_s = (uint32_t)__cvta_generic_to_shared(slot);
@@ -650,15 +649,21 @@ __device__ void decode_groups(const Smem& S, Team& T, const DevStream& d, int g0
             stage_window_bytes(T, buf, d, g, t);
         }
     };
-    for (int i = t; i < kObufWords / 4; i += kTeamThreads)
-        reinterpret_cast<uint4*>(T.obuf)[i] = make_uint4(0, 0, 0, 0);
-    stage_windows(0, g0);
-    cp_async_commit();
-    if (t == 0) {  // thread 0 reads each group's output range one group ahead
-        const GroupRange r0 = group_range(d, g0);
-        T.rng[0][0] = r0.start;
-        T.rng[0][1] = r0.end;
+    // The first group's window bytes and range are fetched while the CTA
+    // sets up the stream's tables (all teams take part; ends with a barrier).
+    if (g0 < g_end) {
+        for (int i = t; i < kObufWords / 4; i += kTeamThreads)
+            reinterpret_cast<uint4*>(T.obuf)[i] = make_uint4(0, 0, 0, 0);
+        stage_windows(0, g0);
+        cp_async_commit();
+        if (t == 0) {  // thread 0 reads each group's output range one group ahead
+            const GroupRange r0 = group_range(d, g0);
+            T.rng[0][0] = r0.start;
+            T.rng[0][1] = r0.end;
+        }
     }
+    setup_stream(S, d);
+    if (g0 >= g_end) return;
     cp_async_wait<0>();
     team_sync(team);
     int buf = 0;
@@ -766,7 +771,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     for (;;) {
         const DevStream& d = B.s[si];
         const long long seg_end = min(hi, d.group_begin + d.n_groups);
-        setup_stream(S, d);
         decode_groups(S, S.team[team], d, (int)(w - d.group_begin) + team, (int)(seg_end - d.group_begin), team, t);
         if (seg_end >= hi) break;
         w = seg_end;
