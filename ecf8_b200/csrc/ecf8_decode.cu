@@ -5,11 +5,11 @@
 // like the reference kernel dfloat/run/decode.cu:16-211, with a different
 // design:
 //
-//  * Persistent CTAs of four teams.  One CTA of 1024 threads per SM holds
-//    one copy of the stream's decode tables in shared memory; each team of
-//    256 threads walks every fourth 4096-byte group (one reference thread
-//    block's worth of stream) of the CTA's range, synchronising on its own
-//    named barrier, so the teams' phases interleave like separate CTAs.
+//  * Persistent CTAs of independent warps.  One CTA of 27 warps per SM holds
+//    one copy of the stream's decode tables in shared memory; each warp
+//    decodes every 27th 4096-byte group (one reference thread block's worth
+//    of stream) of the CTA's range by itself, in eight rounds of 64 windows,
+//    so warps never wait for one another inside a stream.
 //  * Multi-symbol table.  An 8192-entry table indexed by the next 13 stream
 //    bits yields up to six whole symbols, the bits they use and their count,
 //    plus a counter step that advances the bit position, the output nibble
@@ -17,16 +17,17 @@
 //    of the stream's LUTs: ecf8_build_table() derives it once per stream (at
 //    load time) and every CTA copies it into shared memory; without a
 //    prepared table each CTA derives it itself.
-//  * Two windows per thread, one decode pass.  Each thread decodes its two
-//    adjacent 64-bit windows as one continuous run (the first window's gap
-//    gives the start) into a private shared-memory slot of nibbles; a
-//    warp-shuffle scan places each run; slots are funnel-shifted into an
-//    output-ordered nibble buffer.
-//  * Staging and merge.  Each group's bitstream and gaps are staged into
-//    shared memory with 16-byte cp.async one group ahead, its packed
-//    sign+mantissa nibbles at the start of the group; exponent and packed
-//    nibbles are merged 16 elements at a time with byte-permute/logic ops and
-//    written with one 16-byte store.
+//  * Two windows per lane, one decode pass.  Each lane decodes its two
+//    adjacent 64-bit windows of the round as one continuous run (the first
+//    window's gap gives the start) into a private shared-memory slot of
+//    nibbles; a warp-shuffle scan places each run; slots are funnel-shifted
+//    into the warp's output-ordered nibble buffer, whose partial last chunk
+//    carries into the next round.
+//  * Staging and merge.  Each round's bitstream and gaps are staged into
+//    shared memory with 16-byte cp.async one round ahead and its packed
+//    sign+mantissa nibbles are loaded into registers during the decode;
+//    exponent and packed nibbles are merged 16 elements at a time with
+//    byte-permute/logic ops and written with one 16-byte store.
 //
 // No inter-CTA communication, no global scratch, no allocation, no spin-waits.
 
@@ -43,34 +44,39 @@ namespace {
 
 constexpr int kGroupWindows = ECF8_THREADS_PER_BLOCK;   // windows per group (512)
 constexpr int kWindowBytes = ECF8_BYTES_PER_THREAD;     // bytes per window (8)
-constexpr int kTeamThreads = kGroupWindows / 2;         // team size: two windows per thread
-constexpr int kTeams = 4;                               // teams per CTA
-constexpr int kThreads = kTeamThreads * kTeams;         // CTA size
+constexpr int kTableThreads = 256;                      // build_table_kernel block size
+constexpr int kWarps = 27;                              // warps per CTA, each decoding its own groups
+constexpr int kThreads = kWarps * 32;                   // CTA size
 constexpr int kGroupBytes = kGroupWindows * kWindowBytes;  // 4096
+constexpr int kRoundBytes = 64 * kWindowBytes;          // one round: two windows per lane (512 bytes)
+constexpr int kRounds = kGroupBytes / kRoundBytes;      // rounds per group (8)
+constexpr int kRoundStage = kRoundBytes + 16;           // round bytes + look-ahead, 16-byte units
+constexpr int kRoundGaps = 32;                          // gap bytes per round (4 bits per window)
 constexpr int kTabBits = 13;                            // multi-symbol table width
 constexpr int kTabSize = 1 << kTabBits;
 constexpr int kMaxSymsPerEntry = 6;                     // 6 nibbles fit in bits 31..8
 constexpr int kSlotWords = 17;                          // 136 nibbles >= 128 + 4 overshoot (odd stride)
 constexpr int kMaxGroupElems = kGroupWindows * 64;      // one symbol per bit at most
-constexpr int kWinChunks = 1024;                        // 16-element output chunks per obuf window
-constexpr int kObufWords = kWinChunks * 2;              // one window: 16384 nibbles
 constexpr int kLutRows = ECF8_MAX_LUTS - 1;             // decode rows (row 0 + prefixes)
-constexpr int kEncStage = kGroupBytes + 16;             // group bytes + look-ahead, 16-byte units
-constexpr int kGapStage = kGroupWindows / 2;            // 4 bits per window
+constexpr int kGapStage = kGroupWindows / 2;            // gap bytes per group
 
-// One team's buffers.
-struct alignas(16) Team {
-    uint32_t slot[kTeamThreads * kSlotWords];  // per-thread decoded nibbles (MSB first)
-    uint32_t obuf[kObufWords];                 // output-ordered exponent nibbles, one window
-    uint8_t enc[2][kEncStage];                 // staged bitstream, double buffered
-    uint8_t gaps[2][kGapStage];                // staged gaps, double buffered
-    uint32_t wsum[2][kTeamThreads / 32];       // scan: warp totals, double buffered
-    unsigned long long rng[2][2];              // output range [start, end) of the staged groups
+constexpr int kMaxSmem = 232448;                        // opt-in shared memory per CTA (227 KB)
+constexpr int kTablesBytes = kTabSize * 8 + kLutRows * 256 + 256 + kLutRows * 32 + kTabSize * 2;
+constexpr int kRoundNibbles = 15 + 32 * 128;            // a round's codes plus the carried partial chunk
+// Nibble buffer per warp: one whole round's chunks (16-byte units).
+constexpr int kObufWords = (2 * ((kRoundNibbles + 15) / 16) + 3) / 4 * 4;
+
+// One warp's buffers.
+struct alignas(16) WarpBuf {
+    uint32_t slot[32 * kSlotWords];  // per-lane decoded nibbles (MSB first)
+    uint32_t obuf[kObufWords];       // output-ordered exponent nibbles of one round
+    uint8_t enc[2][kRoundStage];     // staged bitstream of a round, double buffered
+    uint8_t gaps[2][kRoundGaps];     // staged gaps of a round, double buffered
 };
-static_assert(offsetof(Team, obuf) % 16 == 0, "obuf must allow 16-byte stores");
-static_assert(offsetof(Team, enc) % 16 == 0 && kEncStage % 16 == 0, "cp.async targets are 16-byte units");
-static_assert(offsetof(Team, gaps) % 16 == 0, "cp.async alignment");
-static_assert(sizeof(Team) % 16 == 0, "teams stay 16-byte aligned");
+static_assert(offsetof(WarpBuf, obuf) % 16 == 0, "obuf must allow 16-byte accesses");
+static_assert(offsetof(WarpBuf, enc) % 16 == 0 && kRoundStage % 16 == 0, "cp.async targets are 16-byte units");
+static_assert(offsetof(WarpBuf, gaps) % 16 == 0, "cp.async alignment");
+static_assert(sizeof(WarpBuf) % 16 == 0, "warp buffers stay 16-byte aligned");
 
 struct alignas(16) Smem {
     uint2 tab[kTabSize];                     // multi-symbol entries (x: entry, y: counter step)
@@ -78,10 +84,13 @@ struct alignas(16) Smem {
     uint8_t lens[256];                       // reference LUT last row: code lengths
     uint32_t chg[kLutRows * 8];              // per row: bit b set if entry b != entry b-1
     uint16_t ends[kTabSize];                 // per entry: bit j set if a symbol other than the last ends at j
-    Team team[kTeams];
+    WarpBuf warp[kWarps];
 };
-static_assert(offsetof(Smem, team) % 16 == 0 && offsetof(Smem, tab) % 16 == 0 && offsetof(Smem, ends) % 16 == 0,
+static_assert(offsetof(Smem, warp) % 16 == 0 && offsetof(Smem, tab) % 16 == 0 && offsetof(Smem, ends) % 16 == 0,
               "vector copies");
+static_assert(sizeof(Smem) <= kMaxSmem, "fits the opt-in shared memory of one CTA");
+static_assert(offsetof(Smem, warp) == kTablesBytes, "table bytes");
+static_assert(kWarps * 32 * 72 <= 65536, "72 registers per thread");
 
 // Shared-memory layout of build_table_kernel: the decode tables only.
 struct alignas(16) TableSmem {
@@ -130,33 +139,8 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
-// Copies bytes [lo, lo + size) of `src` (valid below `limit`) to dst[0, size);
-// size is a multiple of 16.  Asynchronous with cp.async when src + lo is
-// 16-byte aligned, else plain byte loads.
 __device__ __forceinline__ void cp_async16_full(uint32_t dst_s, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst_s), "l"(src) : "memory");
-}
-
-__device__ __forceinline__ void stage(uint8_t* dst, const uint8_t* src, long long lo, int size, long long limit,
-                                      bool async_ok, int t) {
-    if (async_ok && lo + size <= limit) {  // the whole range exists: plain 16-byte copies
-        const uint32_t d0 = (uint32_t)__cvta_generic_to_shared(dst);
-        const uint8_t* s0 = src + lo;
-        for (int i = t * 16; i < size; i += kTeamThreads * 16) cp_async16_full(d0 + i, s0 + i);
-        return;
-    }
-    const long long vl = limit - lo;
-    const int valid = vl < 0 ? 0 : (vl > size ? size : (int)vl);  // bytes of the range that exist
-    const uint8_t* s = src + lo;
-    for (int i = t * 16; i < size; i += kTeamThreads * 16) {
-        const int v = min(max(valid - i, 0), 16);
-        if (async_ok) {
-            cp_async16(dst + i, v ? s + i : src, (uint32_t)v);
-        } else {
-#pragma unroll
-            for (int k = 0; k < 16; ++k) dst[i + k] = k < v ? __ldg(s + i + k) : (uint8_t)0;
-        }
-    }
 }
 
 // ---------------------------------------------------------------------------
@@ -185,11 +169,11 @@ __device__ __forceinline__ uint32_t code_length(const SM& S, uint32_t sym) {
 
 // Bit j set for the end offset of each symbol of entry e (offsets 1..13).
 template <class SM>
-__device__ __forceinline__ uint32_t entry_ends(const SM& S, uint32_t e) {
-    const uint32_t c = (e & 31u) >> 2;
+__device__ __forceinline__ uint32_t entry_ends(const SM& S, uint2 e) {
+    const uint32_t c = (e.y & 31u) >> 2;
     uint32_t pos = 0, mask = 0;
     for (uint32_t i = 0; i < c; ++i) {
-        pos += code_length(S, (e >> (28 - 4 * i)) & 15u);
+        pos += code_length(S, (e.x >> (28 - 4 * i)) & 15u);
         mask |= 1u << pos;
     }
     return mask;
@@ -250,19 +234,25 @@ __device__ void load_luts(SM& S, const DevStream& d) {
 }
 
 // A table entry (64 bits): x = up to six 4-bit symbols, first in bits 31..28,
-// with 4 x count in bits 4..0; y = the counter step (bits << 24) | 4 x count
-// (see decode_run).  All zero: no complete code within the table width.
+// with the bits they use in bits 4..0 (the window's funnel-shift amount);
+// y = the counter step (bits << 24) | 4 x count (see decode_run), whose low
+// five bits are the accumulator's funnel-shift amount.  No complete code
+// within the table width: x = 0 and y = kNoCode, a step that only moves the
+// bit position past the end of any run, so the run loop exits to its
+// long-code path.
+constexpr uint32_t kNoCode = 0x80000000u;
 __device__ __forceinline__ uint2 make_entry(uint32_t syms, uint32_t bits, uint32_t count) {
-    return count ? make_uint2(syms | (4 * count), (bits << 24) | (4 * count)) : make_uint2(0u, 0u);
+    return count ? make_uint2(syms | bits, (bits << 24) | (4 * count)) : make_uint2(0u, kNoCode);
 }
 
 // A prepared entry as read from memory, with every field the decode relies
-// on forced into range (bits 1..kTabBits, count 1..kMaxSymsPerEntry), so a
-// table that ecf8_build_table did not write cannot stall or overrun a run.
+// on forced into range (bits 1..kTabBits, count 1..min(bits, kMaxSymsPerEntry)),
+// so a table that ecf8_build_table did not write cannot stall a run or make
+// it emit more symbols than it has bits.
 __device__ __forceinline__ uint2 sanitize_entry(uint2 e) {
-    const uint32_t b = e.y >> 24, c4 = e.x & 31u;
-    if (e.x == 0 || b == 0 || b > (uint32_t)kTabBits || c4 == 0 || (c4 & 3u) || c4 > 4u * kMaxSymsPerEntry)
-        return make_uint2(0u, 0u);
+    const uint32_t b = e.y >> 24, c4 = e.y & 31u;
+    if (b == 0 || b > (uint32_t)kTabBits || c4 == 0 || (c4 & 3u) || c4 > 4u * kMaxSymsPerEntry || c4 > 4u * b)
+        return make_uint2(0u, kNoCode);
     return make_entry(e.x & 0xffffff00u, b, c4 >> 2);
 }
 
@@ -297,16 +287,16 @@ __device__ void derive_table(SM& S) {
         for (int j = t; j < n; j += (int)blockDim.x) {
             const uint32_t x = (uint32_t)(2 * j + 1) << tz;
             uint32_t sym, len;
-            uint2 ent = make_uint2(0u, 0u);
+            uint2 ent = make_entry(0u, 0u, 0u);
             if (real_code(S, x << (16 - kTabBits), sym, len) && len <= (uint32_t)kTabBits) {
                 uint32_t kept = 0, endk = 0, rest = 0;
                 if (len < (uint32_t)kTabBits) {
-                    const uint32_t ey = S.tab[(x << len) & (kTabSize - 1)].x;
+                    const uint2 ey = S.tab[(x << len) & (kTabSize - 1)];
                     const uint32_t ends = entry_ends(S, ey);
                     kept = min(__popc(ends & ((2u << (kTabBits - len)) - 1u)), kMaxSymsPerEntry - 1);
                     if (kept) {
                         endk = __fns(ends, 0, (int)kept);
-                        rest = (ey >> 4) & (((1u << (4 * kept)) - 1u) << (28 - 4 * kept));
+                        rest = (ey.x >> 4) & (((1u << (4 * kept)) - 1u) << (28 - 4 * kept));
                     }
                 }
                 ent = make_entry(((sym & 15u) << 28) | rest, len + endk, 1 + kept);
@@ -321,7 +311,7 @@ __device__ void derive_table(SM& S) {
 // of decode_run counts the entry's symbols that start before a bit offset).
 template <class SM>
 __device__ __forceinline__ uint16_t entry_start_mask(const SM& S, uint2 e) {
-    return e.x ? (uint16_t)(entry_ends(S, e.x) & ((1u << (e.y >> 24)) - 1u)) : (uint16_t)0;
+    return e.x ? (uint16_t)(entry_ends(S, e) & ((1u << (e.y >> 24)) - 1u)) : (uint16_t)0;
 }
 
 __device__ void build_ends(Smem& S) {
@@ -392,25 +382,41 @@ __device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, u
     uint32_t K = (gap << 24) | ((slot_s >> 2) << 5);
     uint32_t ah = 0, al = 0, elo, ehi;
 #pragma unroll 1
-    do {
+    for (;;) {
+#pragma unroll 1
+        do {
+            const uint32_t sa = (K >> 3) & 0x1ffffcu;
+            lds64(tab_s + ((h >> (32 - kTabBits)) << 3), elo, ehi);
+            ah = __funnelshift_l(al, ah, ehi);  // append the entry's symbols; shift = ehi & 31 = 4 x count
+            al = __funnelshift_l(elo, al, ehi);
+            K += ehi;
+            sts32(sa, __funnelshift_r(al, ah, K));
+            h = __funnelshift_l(m, h, elo);  // consume the entry's bits; shift = elo & 31
+            m = __funnelshift_l(x, m, elo);
+            x = __funnelshift_l(y, x, elo);
+            y = __funnelshift_l(z, y, elo);
+            z = __funnelshift_l(0u, z, elo);
+        } while (K < (128u << 24));
+        if (__builtin_expect(ehi != kNoCode, 1)) break;
+        // No complete code within the table width (decode.cu:86-91): the
+        // no-code step left everything but the bit position alone.
+        K -= kNoCode;
+        const uint32_t sym = lut_symbol(S, h);
+        const uint32_t len = min(code_length(S, sym), 31u);
+        elo = ((sym & 15u) << 28) | len;
+        ehi = (len << 24) | 4u;
         const uint32_t sa = (K >> 3) & 0x1ffffcu;
-        lds64(tab_s + ((h >> (32 - kTabBits)) << 3), elo, ehi);
-        if (__builtin_expect(elo == 0, 0)) {  // no complete code within the table width (decode.cu:86-91)
-            const uint32_t sym = lut_symbol(S, h);
-            elo = ((sym & 15u) << 28) | 4u;
-            ehi = (min(code_length(S, sym), 32u) << 24) | 4u;
-        }
-        ah = __funnelshift_l(al, ah, elo);  // append the entry's symbols; shift = elo & 31 = 4 x count
-        al = __funnelshift_l(elo, al, elo);
+        ah = __funnelshift_l(al, ah, ehi);
+        al = __funnelshift_l(elo, al, ehi);
         K += ehi;
         sts32(sa, __funnelshift_r(al, ah, K));
-        const uint32_t b = ehi >> 24;
-        h = __funnelshift_l(m, h, b);
-        m = __funnelshift_l(x, m, b);
-        x = __funnelshift_l(y, x, b);
-        y = __funnelshift_l(z, y, b);
-        z <<= b;
-    } while (K < (128u << 24));
+        h = __funnelshift_l(m, h, elo);
+        m = __funnelshift_l(x, m, elo);
+        x = __funnelshift_l(y, x, elo);
+        y = __funnelshift_l(z, y, elo);
+        z = __funnelshift_l(0u, z, elo);
+        if (K >= (128u << 24)) break;
+    }
     const uint32_t m4 = K & 31u;
     const uint32_t words = ((K >> 5) & 0x7ffffu) - (slot_s >> 2);
     if (m4) sts32(slot_s + 4 * words, al << (32 - m4));
@@ -422,10 +428,11 @@ __device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, u
     if (room < (uint32_t)kTabBits) {
         const uint32_t b3 = __byte_perm(lds32(tail_s), 0, 0x0123), b4 = __byte_perm(lds32(tail_s + 4), 0, 0x0123);
         const uint32_t idx = __funnelshift_l(b4, b3, 32u - room) >> (32 - kTabBits);
-        const uint32_t keep = 1u + __popc(S.ends[idx] & ((1u << room) - 1u));
-        n -= ((elo & 31u) >> 2) - keep;
+        const uint32_t c = (ehi & 31u) >> 2;
+        const uint32_t keep = min(1u + __popc(S.ends[idx] & ((1u << room) - 1u)), c);
+        n -= c - keep;
     }
-    return n;
+    return min(n, 128u - gap);  // codes start at distinct bits of [gap, 128); binds only for a corrupt table
 }
 
 // Bitwise select: bits of x where m is 1, bits of y where m is 0 (one LOP3).
@@ -464,15 +471,6 @@ __device__ __forceinline__ GroupRange group_range(const DevStream& d, long long 
     return {start, end};
 }
 
-__device__ __forceinline__ void stage_window_bytes(Team& T, int buf, const DevStream& d, long long g, int t) {
-    stage(T.enc[buf], d.encoded, g * kGroupBytes, kEncStage, d.n_bytes, d.async_ok, t);
-    stage(T.gaps[buf], d.gaps, g * kGapStage, kGapStage, g * kGapStage + kGapStage, d.async_ok, t);
-}
-
-__device__ __forceinline__ void team_sync(int team) {
-    asm volatile("bar.sync %0, %1;" ::"r"(team + 1), "n"(kTeamThreads) : "memory");
-}
-
 __device__ __forceinline__ int find_stream(const DevStream* s, int from, long long w) {
     while (w >= s[from].group_begin + s[from].n_groups) ++from;
     return from;
@@ -490,219 +488,213 @@ __device__ __forceinline__ uint2 packed8(const DevStream& d, unsigned long long 
 }
 
 // Copies run nibbles [dpos, dpos + n) (output positions relative to the
-// group's base) from the run's slot into the nibble buffer, whose word 0 is
-// output word wlo.  The run's first and last words are shared with the
-// neighbouring runs (atomicOr into the zeroed buffer); the words in between
-// are its own.  With WIN, words outside the buffer's window are skipped (the
-// unsigned window offsets wrap for words before it).  Reading slot[nw] when
-// nw is the slot size stays in shared memory (the next slot or the buffer)
-// and is masked off by `tail`.
-template <bool WIN>
-__device__ __forceinline__ void place_run(uint32_t* obuf, const uint32_t* slot, uint32_t dpos, uint32_t n,
-                                          uint32_t wlo) {
+// nibble buffer's word 0) from the run's slot into the buffer.  The run's
+// first and last words are shared with the neighbouring runs (atomicOr into
+// the zeroed buffer); the words in between are its own.  Reading slot[nw]
+// when nw is the slot size stays in shared memory (the next slot or the
+// buffer) and is masked off by `tail`.
+__device__ __forceinline__ void place_run(uint32_t* obuf, const uint32_t* slot, uint32_t dpos, uint32_t n) {
     const uint32_t e = dpos + n;
     const uint32_t nw = ((e - 1) >> 3) - (dpos >> 3);  // words after the first
     const uint32_t sh = (dpos & 7) * 4;
     const uint32_t tail = 0xffffffffu << (((8u - (e & 7)) * 4) & 31);
-    const uint32_t o0 = (dpos >> 3) - wlo;
+    const uint32_t o0 = dpos >> 3;
     uint32_t prev = slot[0];
-    if (!WIN || o0 < (uint32_t)kObufWords) atomicOr(obuf + o0, (prev >> sh) & (nw ? 0xffffffffu : tail));
+    atomicOr(obuf + o0, (prev >> sh) & (nw ? 0xffffffffu : tail));
     uint32_t q = 1;
     for (; q + 1 < nw; q += 2) {
         const uint32_t c0 = slot[q], c1 = slot[q + 1];
-        if (!WIN || o0 + q < (uint32_t)kObufWords) obuf[o0 + q] = __funnelshift_r(c0, prev, sh);
-        if (!WIN || o0 + q + 1 < (uint32_t)kObufWords) obuf[o0 + q + 1] = __funnelshift_r(c1, c0, sh);
+        obuf[o0 + q] = __funnelshift_r(c0, prev, sh);
+        obuf[o0 + q + 1] = __funnelshift_r(c1, c0, sh);
         prev = c1;
     }
     if (q < nw) {
         const uint32_t c0 = slot[q];
-        if (!WIN || o0 + q < (uint32_t)kObufWords) obuf[o0 + q] = __funnelshift_r(c0, prev, sh);
+        obuf[o0 + q] = __funnelshift_r(c0, prev, sh);
         prev = c0;
     }
-    if (nw && (!WIN || o0 + nw < (uint32_t)kObufWords))
-        atomicOr(obuf + o0 + nw, __funnelshift_r(slot[nw], prev, sh) & tail);
+    if (nw) atomicOr(obuf + o0 + nw, __funnelshift_r(slot[nw], prev, sh) & tail);
 }
 
-// Merges and stores output chunks [c_lo, c_hi) of the group (16 elements
-// each, from base); the nibble buffer holds chunk c_lo at word 0 and every
-// word read is zeroed again for the next group.  Packed nibbles are read from
-// global memory.  Chunks wholly inside the group's range [rs, re) are stored
-// 16 bytes at a time when the output is aligned; the group's first and last
-// chunk may be partial (shared with the neighbouring groups) and are written
-// byte by byte by two threads, as every chunk is for unaligned output.
-__device__ __forceinline__ void merge_chunks(Team& T, const DevStream& d, unsigned long long base, uint32_t rs,
-                                             uint32_t re, int c_lo, int c_hi, int t) {
-    const int first_full = rs ? 1 : 0;
-    const int c_first = max(first_full, c_lo);
-    const int c_end = min((int)(re >> 4), c_hi);  // chunks [c_first, c_end) are full
-    uint2* ew2 = reinterpret_cast<uint2*>(T.obuf);
-    if (d.out16) {
-        uint4* ob = reinterpret_cast<uint4*>(d.out + base);
-        for (int c = c_first + t; c < c_end; c += kTeamThreads) {
-            const uint2 ew = ew2[c - c_lo];
-            ew2[c - c_lo] = make_uint2(0u, 0u);
-            const uint2 pw = packed8(d, (base >> 1) + 8ull * c);
-            uint4 o;
-            merge8(ew.x, pw.x, o.x, o.y);
-            merge8(ew.y, pw.y, o.z, o.w);
-            ob[c] = o;
+// Stages round r of group g (its 512 stream bytes plus 16 bytes of
+// look-ahead, and its 32 gap bytes) into buffer b of the warp, zero-filled
+// past the end of the stream.  cp.async when the stream's buffers are 16-byte
+// aligned, plain loads otherwise.  The lanes read each other's bytes only
+// after the warp's next __syncwarp.
+__device__ __forceinline__ void stage_round(WarpBuf& W, const DevStream& d, int b, int g, int r, int lane) {
+    const long long lo = (long long)g * kGroupBytes + (long long)r * kRoundBytes;
+    const uint32_t eb = (uint32_t)__cvta_generic_to_shared(W.enc[b]);
+    if (d.async_ok && lo + kRoundStage <= d.n_bytes) {
+        cp_async16_full(eb + 16 * lane, d.encoded + lo + 16 * lane);
+        if (lane == 0) cp_async16_full(eb + kRoundBytes, d.encoded + lo + kRoundBytes);
+    } else {
+        const long long vl = d.n_bytes - lo;
+        for (int i = 16 * lane; i < kRoundStage; i += 32 * 16) {
+            const int v = (int)min(max(vl - i, 0ll), 16ll);  // bytes of this unit inside the stream
+            if (d.async_ok) {
+                cp_async16(W.enc[b] + i, v ? d.encoded + lo + i : d.encoded, (uint32_t)v);
+            } else {
+#pragma unroll
+                for (int k = 0; k < 16; ++k) W.enc[b][i + k] = k < v ? __ldg(d.encoded + lo + i + k) : (uint8_t)0;
+            }
         }
     }
-    const int last = (int)(re >> 4);
-    int c = -1;
-    if (!d.out16) {
-        c = c_lo + t;
-    } else if (t == 0 && rs && c_lo == 0) {
-        c = 0;
-    } else if (t == 1 && (re & 15) && last >= first_full && last >= c_lo && last < c_hi) {
-        c = last;
-    }
-    for (; c >= 0 && c < c_hi; c = d.out16 ? -1 : c + kTeamThreads) {
-        const uint32_t e0 = 16u * c;
-        const uint2 ew = ew2[c - c_lo];
-        ew2[c - c_lo] = make_uint2(0u, 0u);
-        const uint2 pw = packed8(d, (base >> 1) + 8ull * c);
-        uint32_t ow[4];
-        merge8(ew.x, pw.x, ow[0], ow[1]);
-        merge8(ew.y, pw.y, ow[2], ow[3]);
-        uint8_t* dst = d.out + base + e0;
-#pragma unroll
-        for (int k = 0; k < 16; ++k)
-            if (e0 + k >= rs && e0 + k < re) dst[k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
+    const long long glo = (long long)g * kGapStage + (long long)r * kRoundGaps;  // gaps exist for every group
+    if (d.async_ok) {
+        if (lane < kRoundGaps / 16)
+            cp_async16_full((uint32_t)__cvta_generic_to_shared(W.gaps[b]) + 16 * lane, d.gaps + glo + 16 * lane);
+    } else {
+        W.gaps[b][lane] = __ldg(d.gaps + glo + lane);
     }
 }
 
-// Merge fast path: one window, 16-byte aligned output and packed nibbles.
-// The packed words of a thread's full chunks (c_first + t + 256 k, k < 4) were
-// loaded into `pw` at the start of the group; every nibble-buffer word read is
-// zeroed again.  Threads 0 and 1 write the group's partial first and last
-// chunk byte by byte.
-__device__ __forceinline__ void merge_fast(Team& T, const DevStream& d, unsigned long long base, uint32_t rs,
-                                           uint32_t re, int t, const uint2 (&pw)[4]) {
-    const int c_first = rs ? 1 : 0;
-    const int c_end = (int)(re >> 4);  // chunks [c_first, c_end) are full
-    uint2* ew2 = reinterpret_cast<uint2*>(T.obuf);
-    uint8_t* outb = d.out + base;
-    uint4* ob = reinterpret_cast<uint4*>(outb);
+// Packed words of chunks C + lane + 32k (k < 4) of the group at `base`,
+// those entirely below the group's end `re`; loaded while the round decodes.
+__device__ __forceinline__ void prefetch_packed(uint2 (&pw)[4], const DevStream& d, unsigned long long base,
+                                                uint32_t C, uint32_t re, int lane) {
+    const uint2* src = reinterpret_cast<const uint2*>(d.packed + (base >> 1));
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const int c = c_first + t + k * kTeamThreads;
-        if (c < c_end) {
-            const uint2 ew = ew2[c];
-            ew2[c] = make_uint2(0u, 0u);
-            uint4 o;
-            merge8(ew.x, pw[k].x, o.x, o.y);
-            merge8(ew.y, pw[k].y, o.z, o.w);
-            ob[c] = o;
-        }
-    }
-    if (t < 2) {
-        const int c = t == 0 ? (rs ? 0 : -1) : ((re & 15) && c_end >= c_first ? c_end : -1);
-        if (c >= 0) {
-            const uint2 ew = ew2[c];
-            ew2[c] = make_uint2(0u, 0u);
-            const uint2 p = packed8(d, (base >> 1) + 8ull * c);
-            uint32_t ow[4];
-            merge8(ew.x, p.x, ow[0], ow[1]);
-            merge8(ew.y, p.y, ow[2], ow[3]);
-            const uint32_t e0 = 16u * c;
-#pragma unroll
-            for (int k = 0; k < 16; ++k)
-                if (e0 + k >= rs && e0 + k < re) outb[e0 + k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
-        }
+        const uint32_t c = C + lane + 32 * k;
+        pw[k] = c < (re >> 4) ? __ldg(src + c) : make_uint2(0u, 0u);
     }
 }
 
-// One team decodes groups g0, g0 + kTeams, ... below g_end of stream d.  t is
-// the thread's index in the team; the team's barrier is named barrier team+1.
-//
-// Two barriers per group.  The first (after the decode) publishes the warp
-// totals of the scan, the next group's staged bitstream (each thread waits for
-// its own copies just before it) and the next group's range (read by thread 0
-// one group ahead); the second publishes the nibble buffer for the merge.  No
-// barrier is needed at the top of a group: the staging buffers and warp
-// totals are double buffered, the slots are private, and the merge zeroes
-// every nibble-buffer word it reads, so the buffer is zero again before any
-// thread passes the next group's first barrier.  Interior groups (whole
-// staging window inside the stream, 16-byte aligned buffers, one window) load
-// their packed nibbles into registers at the start of the group and take the
-// fast merge; the stream's last groups and unaligned streams take the
-// general paths.
-__device__ void decode_groups(Smem& S, Team& T, const DevStream& d, int g0, int g_end, int team, int t) {
-    const int lane = t & 31, warp = t >> 5;
-    uint32_t* slot = T.slot + t * kSlotWords;
-    const uint32_t slot_s = (uint32_t)__cvta_generic_to_shared(slot);
-    const long long n_bytes = d.n_bytes;
-    // Groups below g_fast have their whole 4112-byte staging window inside the stream.
-    const int g_fast = (d.async_ok && n_bytes >= kEncStage) ? (int)((n_bytes - kEncStage) / kGroupBytes) + 1 : 0;
-    const uint32_t enc_s0 = (uint32_t)__cvta_generic_to_shared(T.enc[0]);
-    const uint32_t gaps_s0 = (uint32_t)__cvta_generic_to_shared(T.gaps[0]);
-    auto stage_windows = [&](int buf, int g) {
-        if (g < g_fast) {
-            const uint8_t* es = d.encoded + (long long)g * kGroupBytes;
-            const uint8_t* gs = d.gaps + (long long)g * kGapStage;
-            const uint32_t eb = enc_s0 + buf * kEncStage, gb = gaps_s0 + buf * kGapStage;
-            cp_async16_full(eb + 16 * t, es + 16 * t);
-            if (t == 0) cp_async16_full(eb + kGroupBytes, es + kGroupBytes);
-            if (t < kGapStage / 16) cp_async16_full(gb + 16 * t, gs + 16 * t);
-        } else {
-            stage_window_bytes(T, buf, d, g, t);
-        }
-    };
-    // The first group's window bytes and range are fetched while the CTA
-    // sets up the stream's tables (all teams take part; ends with a barrier).
-    if (g0 < g_end) {
-        for (int i = t; i < kObufWords / 4; i += kTeamThreads)
-            reinterpret_cast<uint4*>(T.obuf)[i] = make_uint4(0, 0, 0, 0);
-        stage_windows(0, g0);
-        cp_async_commit();
-        if (t == 0) {  // thread 0 reads each group's output range one group ahead
-            const GroupRange r0 = group_range(d, g0);
-            T.rng[0][0] = r0.start;
-            T.rng[0][1] = r0.end;
+// Merges output chunk c (16 elements from base + 16c) and stores the
+// elements inside the group's range [rs, re) byte by byte.
+__device__ __forceinline__ void store_bytes(const DevStream& d, unsigned long long base, uint32_t c, uint2 ew,
+                                            uint2 p, uint32_t rs, uint32_t re) {
+    uint32_t ow[4];
+    merge8(ew.x, p.x, ow[0], ow[1]);
+    merge8(ew.y, p.y, ow[2], ow[3]);
+    uint8_t* dst = d.out + base;
+    const uint32_t e0 = 16u * c;
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+        if (e0 + k >= rs && e0 + k < re) dst[e0 + k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
+}
+
+// Merges and stores the round's complete chunks [C, Cn); the nibble buffer
+// holds chunk C at word 0 and every word read is zeroed again.  Chunk
+// C + lane + 32k takes the prefetched packed word pw[k]; chunks from C + 128
+// on (highly compressed rounds) load theirs here.  Lane 0 merges chunk C and
+// then moves the round's partial last chunk Cn (if any) to word 0 for the
+// next round, so no other lane touches words 0..1.  The group's partial first
+// chunk (c = 0 when rs > 0) and all chunks of unaligned streams are stored
+// byte by byte.
+__device__ __forceinline__ void merge_round(WarpBuf& W, const DevStream& d, unsigned long long base, uint32_t rs,
+                                            uint32_t re, uint32_t C, uint32_t Cn, uint32_t Pn, int lane, bool fast,
+                                            const uint2 (&pw)[4]) {
+    uint2* ew2 = reinterpret_cast<uint2*>(W.obuf);
+    uint4* ob = reinterpret_cast<uint4*>(d.out + base);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t c = C + lane + 32 * k;
+        if (c < Cn) {
+            const uint2 ew = ew2[c - C];
+            ew2[c - C] = make_uint2(0u, 0u);
+            if (fast && (c || !rs)) {
+                uint4 o;
+                merge8(ew.x, pw[k].x, o.x, o.y);
+                merge8(ew.y, pw[k].y, o.z, o.w);
+                ob[c] = o;
+            } else {
+                store_bytes(d, base, c, ew, fast ? pw[k] : packed8(d, (base >> 1) + 8ull * c), rs, re);
+            }
         }
     }
+    for (uint32_t c = C + 128 + lane; c < Cn; c += 32) {
+        const uint2 ew = ew2[c - C];
+        ew2[c - C] = make_uint2(0u, 0u);
+        const uint2 p = packed8(d, (base >> 1) + 8ull * c);
+        if (fast) {
+            uint4 o;
+            merge8(ew.x, p.x, o.x, o.y);
+            merge8(ew.y, p.y, o.z, o.w);
+            ob[c] = o;
+        } else {
+            store_bytes(d, base, c, ew, p, rs, re);
+        }
+    }
+    if (lane == 0 && Cn > C && (Pn & 15u)) {
+        ew2[0] = ew2[Cn - C];
+        ew2[Cn - C] = make_uint2(0u, 0u);
+    }
+}
+
+// After a group's last round: chunks [Cn, ceil(re / 16)) -- the partial last
+// chunk, whose nibbles sit at word 0, and any chunk the stream's codes did not
+// reach (exponent 0) -- stored byte by byte; word 0 is zeroed again.
+__device__ __forceinline__ void flush_group(WarpBuf& W, const DevStream& d, unsigned long long base, uint32_t rs,
+                                            uint32_t re, uint32_t Cn, int lane) {
+    uint2* ew2 = reinterpret_cast<uint2*>(W.obuf);
+    const uint32_t n_chunks = (re + 15) >> 4;
+    for (uint32_t c = Cn + lane; c < n_chunks; c += 32) {
+        uint2 ew = make_uint2(0u, 0u);
+        if (c == Cn) {
+            ew = ew2[0];
+            ew2[0] = make_uint2(0u, 0u);
+        }
+        store_bytes(d, base, c, ew, packed8(d, (base >> 1) + 8ull * c), rs, re);
+    }
+}
+
+// One warp decodes groups g0, g0 + kWarps, ... below g_end of stream d, each
+// in eight rounds of 64 windows: lane i decodes windows 2i and 2i + 1 of the
+// round as one run into its slot, a warp-shuffle scan places the runs, and
+// the round's complete 16-element chunks are merged and stored.  The output
+// position P (relative to the group's 16-aligned base) carries from round to
+// round, and with it the partial chunk that holds P.  Only __syncwarp
+// orders the lanes: one after the placement (nibble buffer complete), one
+// after the merge (buffer zero again but for the carried chunk, next round's
+// staged bytes visible).  The next round is staged and its packed words are
+// loaded while the current round decodes.
+__device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int g0, int g_end, int lane) {
+    uint32_t* slot = W.slot + lane * kSlotWords;
+    const uint32_t slot_s = (uint32_t)__cvta_generic_to_shared(slot);
+    const uint32_t enc_s0 = (uint32_t)__cvta_generic_to_shared(W.enc[0]);
+    const long long n_bytes = d.n_bytes;
+    const bool fast = d.out16 && d.async_ok;
+    // The first round's bytes and the first group's range are fetched while
+    // the CTA sets up the stream's tables (all warps take part; ends with a barrier).
+    GroupRange rg{0, 0};
+    if (g0 < g_end) {
+        for (int i = lane; i < kObufWords / 4; i += 32) reinterpret_cast<uint4*>(W.obuf)[i] = make_uint4(0, 0, 0, 0);
+        stage_round(W, d, 0, g0, 0, lane);
+        rg = group_range(d, g0);
+    }
+    cp_async_commit();
     setup_stream(S, d);
     if (g0 >= g_end) return;
     cp_async_wait<0>();
-    team_sync(team);
-    int buf = 0;
-    for (int g = g0; g < g_end; g += kTeams, buf ^= 1) {
-        const unsigned long long start = T.rng[buf][0], end = T.rng[buf][1];
-        const unsigned long long base = start & ~15ull;
-        const uint32_t rs = (uint32_t)(start - base), re = (uint32_t)(end - base);  // range rel. to base
-        const int n_chunks = (int)((re + 15) >> 4);
-        const bool fast = d.out16 && d.async_ok && n_chunks <= kWinChunks;
+    __syncwarp();
 
-        // Stage the next group's window bytes; read its output range.
-        GroupRange rn{0, 0};
-        if (g + kTeams < g_end) {
-            stage_windows(buf ^ 1, g + kTeams);
-            if (t == 0) rn = group_range(d, g + kTeams);
-        }
+    int g = g0, r = 0, buf = 0;
+    unsigned long long base = rg.start & ~15ull;
+    uint32_t rs = (uint32_t)(rg.start - base), re = (uint32_t)(rg.end - base), P = rs;
+    GroupRange rn = g + kWarps < g_end ? group_range(d, g + kWarps) : GroupRange{0, 0};
+    uint2 pw[4];
+    if (fast) prefetch_packed(pw, d, base, 0, re, lane);
+#pragma unroll 1
+    for (;;) {
+        const bool last_round = r == kRounds - 1;
+        if (!last_round)
+            stage_round(W, d, buf ^ 1, g, r + 1, lane);
+        else if (g + kWarps < g_end)
+            stage_round(W, d, buf ^ 1, g + kWarps, 0, lane);
         cp_async_commit();
-        // This thread's packed words for the fast merge, in flight during the decode.
-        uint2 pw[4];
-        if (fast) {
-            const int c_first = rs ? 1 : 0, c_end = (int)(re >> 4);
-            const uint2* src = reinterpret_cast<const uint2*>(d.packed + (base >> 1));
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int c = c_first + t + k * kTeamThreads;
-                pw[k] = c < c_end ? __ldg(src + c) : make_uint2(0u, 0u);
-            }
-        }
 
-        // --- decode this thread's window pair ---
+        // --- decode this lane's window pair ---
         uint32_t count = 0;
-        const long long rem = n_bytes - (long long)g * kGroupBytes;  // stream bytes from this group on
-        if (rem > 16 * t) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(T.enc[buf] + 16 * t);
-            const uint32_t r4 = *reinterpret_cast<const uint32_t*>(T.enc[buf] + 16 * t + 16);
+        const long long rem = n_bytes - (long long)g * kGroupBytes - (long long)r * kRoundBytes;
+        if (rem > 16 * lane) {
+            const uint8_t* e = W.enc[buf] + 16 * lane;
+            const uint4 raw = *reinterpret_cast<const uint4*>(e);
+            const uint32_t r4 = *reinterpret_cast<const uint32_t*>(e + 16);
             count = decode_run(S, slot_s, __byte_perm(raw.x, 0, 0x0123), __byte_perm(raw.y, 0, 0x0123),
                                __byte_perm(raw.z, 0, 0x0123), __byte_perm(raw.w, 0, 0x0123),
-                               __byte_perm(r4, 0, 0x0123), T.gaps[buf][t] >> 4,
-                               enc_s0 + buf * kEncStage + 16 * t + 12);
+                               __byte_perm(r4, 0, 0x0123), W.gaps[buf][lane] >> 4,
+                               enc_s0 + buf * kRoundStage + 16 * lane + 12);
         }
         // A pair wholly past n_bytes only follows the last real code: it places nothing.
 
@@ -713,74 +705,65 @@ __device__ void decode_groups(Smem& S, Team& T, const DevStream& d, int g0, int 
             const uint32_t y = __shfl_up_sync(0xffffffffu, v, o);
             if (lane >= o) v += y;
         }
-        if (lane == 31) T.wsum[buf][warp] = v;
-        if (t == 0 && g + kTeams < g_end) {
-            T.rng[buf ^ 1][0] = rn.start;
-            T.rng[buf ^ 1][1] = rn.end;
-        }
-        cp_async_wait<0>();  // this thread's copies of the next group's window bytes
-        team_sync(team);
-        uint32_t ws = lane < kTeamThreads / 32 ? T.wsum[buf][lane] : 0u;
-#pragma unroll
-        for (int o = 1; o < kTeamThreads / 32; o <<= 1) {
-            const uint32_t y = __shfl_up_sync(0xffffffffu, ws, o);
-            if (lane >= o) ws += y;
-        }
-        const uint32_t wbase = __shfl_sync(0xffffffffu, ws, (warp + 31) & 31);
-        const uint32_t excl = v - count + (warp ? wbase : 0u);
-
-        // --- place the runs' nibbles in output order, merge, store ---
-        // A group's output goes through the nibble buffer in windows of
-        // kWinChunks chunks; all but highly compressed groups take one.
-        const uint32_t dpos = rs + excl;
+        const uint32_t total = __shfl_sync(0xffffffffu, v, 31);
+        const uint32_t C = P >> 4;
+        const uint32_t dpos = P + v - count;
         const uint32_t n_place = (count && dpos < re) ? min(count, re - dpos) : 0u;
-        if (n_chunks <= kWinChunks) {
-            if (n_place) place_run<false>(T.obuf, slot, dpos, n_place, 0);
-            team_sync(team);
-            if (fast)
-                merge_fast(T, d, base, rs, re, t, pw);
-            else
-                merge_chunks(T, d, base, rs, re, 0, n_chunks, t);
-        } else {
-            for (int c_lo = 0; c_lo < n_chunks; c_lo += kWinChunks) {
-                if (c_lo) team_sync(team);  // the previous window is merged (and zeroed)
-                if (n_place) place_run<true>(T.obuf, slot, dpos, n_place, (uint32_t)c_lo * 2);
-                team_sync(team);
-                merge_chunks(T, d, base, rs, re, c_lo, min(n_chunks, c_lo + kWinChunks), t);
-            }
+        const uint32_t Pn = min(P + total, re);
+        const uint32_t Cn = Pn >> 4;
+        if (n_place) place_run(W.obuf, slot, dpos - 16u * C, n_place);
+        __syncwarp();
+        merge_round(W, d, base, rs, re, C, Cn, Pn, lane, fast, pw);
+        cp_async_wait<0>();  // this lane's copies of the next round
+        __syncwarp();
+        P = Pn;
+        buf ^= 1;
+        if (!last_round) {
+            ++r;
+            if (fast) prefetch_packed(pw, d, base, Cn, re, lane);
+            continue;
         }
+        flush_group(W, d, base, rs, re, Cn, lane);
+        __syncwarp();
+        g += kWarps;
+        if (g >= g_end) break;
+        r = 0;
+        base = rn.start & ~15ull;
+        rs = (uint32_t)(rn.start - base);
+        re = (uint32_t)(rn.end - base);
+        P = rs;
+        if (g + kWarps < g_end) rn = group_range(d, g + kWarps);
+        if (fast) prefetch_packed(pw, d, base, 0, re, lane);
     }
-    cp_async_wait<0>();
 }
 
 template <int MAXS>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ Batch<MAXS> B) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem& S = *reinterpret_cast<Smem*>(smem_raw);
-    const int team = threadIdx.x / kTeamThreads;
-    const int t = threadIdx.x - team * kTeamThreads;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long long total = B.total_groups;
     const long long lo = (long long)blockIdx.x * total / gridDim.x;
     const long long hi = (long long)(blockIdx.x + 1) * total / gridDim.x;
     if (lo >= hi) return;
 
     // The CTA's range [lo, hi) in per-stream segments: the tables of one
-    // stream at a time, each team taking every third group of the segment.
+    // stream at a time, each warp taking every kWarps-th group of the segment.
     int si = find_stream(B.s, 0, lo);
     long long w = lo;
     for (;;) {
         const DevStream& d = B.s[si];
         const long long seg_end = min(hi, d.group_begin + d.n_groups);
-        decode_groups(S, S.team[team], d, (int)(w - d.group_begin) + team, (int)(seg_end - d.group_begin), team, t);
+        decode_warp(S, S.warp[warp], d, (int)(w - d.group_begin) + warp, (int)(seg_end - d.group_begin), lane);
         if (seg_end >= hi) break;
         w = seg_end;
         si = find_stream(B.s, si, w);
-        __syncthreads();  // every team is done with this stream's tables
+        __syncthreads();  // every warp is done with this stream's tables
     }
 }
 
 // One CTA derives a stream's multi-symbol table and writes it to `table`.
-__global__ void __launch_bounds__(kTeamThreads, 1) build_table_kernel(const uint8_t* luts, int n_luts,
+__global__ void __launch_bounds__(kTableThreads, 1) build_table_kernel(const uint8_t* luts, int n_luts,
                                                                        uint32_t* table) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     TableSmem& S = *reinterpret_cast<TableSmem*>(smem_raw);
@@ -970,7 +953,7 @@ int ecf8_build_table(const uint8_t* luts, int n_luts, uint32_t* table, void* cud
     ecf8::DeviceInfo info;
     int st = ecf8::device_info(&info);
     if (st != ECF8_OK) return st;
-    ecf8::build_table_kernel<<<1, ecf8::kTeamThreads, sizeof(ecf8::TableSmem), (cudaStream_t)cuda_stream>>>(
+    ecf8::build_table_kernel<<<1, ecf8::kTableThreads, sizeof(ecf8::TableSmem), (cudaStream_t)cuda_stream>>>(
         luts, n_luts, table);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return ecf8::cuda_fail(e);
