@@ -288,3 +288,67 @@ def test_batch_mixing_prepared_and_derived_tables(cuda_device):
     torch.cuda.synchronize()
     for n, s, o in zip(names, ss, outs):
         assert np.array_equal(o.cpu().numpy(), s["fp8"]), n
+
+
+def _skewed_stream(oracle, rng, n):
+    """A code table from power-of-two counts (codes of 1 to 16 bits) with
+    data drawn uniformly over the same 16 symbols: about a sixth of the codes
+    are longer than the 13-bit table, so table steps often end the run loop
+    for the two-level LUT, at run ends too."""
+    from ecf8_b200 import codec
+    from helpers import fp8_from_exponents, table_to_arrays
+    cnt = {int(s): 1 << i for i, s in enumerate(rng.permutation(16))}
+    table = codec.huffman_code_table(cnt)
+    luts = codec.get_luts_from_huffman_table(table).numpy()
+    bits, vals, eb, ev = table_to_arrays(table)
+    e = rng.integers(0, 16, n).astype(np.uint8)
+    enc, gaps, op = oracle.encode(e, bits, vals, eb, ev)
+    fp8 = fp8_from_exponents(e, rng)
+    _, packed = oracle.split(fp8)
+    return {"fp8": fp8, "luts": luts, "encoded": enc, "packed": packed, "gaps": gaps,
+            "output_positions": op, "table": table, "max_bits": int(bits.max())}
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_long_codes_everywhere(cuda_device, oracle_mod, seed):
+    from ecf8_b200.run import build_decode_table, decode_stream
+    rng = np.random.default_rng(700 + seed)
+    s = _skewed_stream(oracle_mod, rng, 200000 + 2 * seed)
+    assert s["max_bits"] > 13
+    d = to_device(s, cuda_device)
+    derived, guard = decode_guarded(d, s["fp8"].size, cuda_device)
+    assert np.all(guard == GUARD)
+    assert np.array_equal(derived, s["fp8"])
+    out = decode_stream(d["luts"], d["encoded"], d["packed_other_4bits"], d["output_positions"], d["gaps"],
+                        table=build_decode_table(d["luts"]))
+    assert np.array_equal(out.view(torch.uint8).cpu().numpy(), s["fp8"])
+    if seed == 0:
+        assert np.array_equal(run_reference_kernel(s, cuda_device), s["fp8"])
+
+
+def test_corrupt_prepared_table_stays_in_bounds(cuda_device):
+    """A table ecf8_build_table did not write (random words; random entries
+    with in-range bit counts but more symbols than bits; random end masks)
+    must not make the kernel stall or touch memory outside its buffers."""
+    from ecf8_b200 import _lib
+    from ecf8_b200.run import decode_stream
+    rng = np.random.default_rng(9)
+    s = load_golden("gauss_block128")
+    d = to_device(s, cuda_device)
+    n = s["fp8"].size
+    words = _lib.TABLE_BYTES // 4
+    for trial in range(4):
+        t = rng.integers(0, 2 ** 32, words, dtype=np.uint64).astype(np.uint32)
+        if trial % 2:  # entries: bits 1..13, 1..6 symbols (often more than bits)
+            ent = t[:16384].reshape(8192, 2)
+            b = rng.integers(1, 14, 8192).astype(np.uint32)
+            c = rng.integers(1, 7, 8192).astype(np.uint32)
+            ent[:, 0] = (ent[:, 0] & 0xffffff00) | b
+            ent[:, 1] = (b << 24) | (4 * c)
+        table = torch.from_numpy(t.view(np.int32).copy()).to(cuda_device)
+        buf = torch.full((n + 64,), GUARD, dtype=torch.uint8, device=cuda_device)
+        decode_stream(d["luts"], d["encoded"], d["packed_other_4bits"], d["output_positions"], d["gaps"],
+                      buf[32:32 + n], table=table)
+        torch.cuda.synchronize()
+        b = buf.cpu().numpy()
+        assert np.all(b[:32] == GUARD) and np.all(b[32 + n:] == GUARD)

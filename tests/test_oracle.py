@@ -99,3 +99,23 @@ def test_dahuffman_standin_gives_complete_prefix_codes():
         assert len(t) == k + 1
         assert abs(sum(2.0 ** -b for b, _ in t.values()) - 1.0) < 1e-12
         assert max(b for b, _ in t.values()) <= 16
+
+
+def test_oracle_decodes_codes_up_to_16_bits(oracle_mod):
+    """Power-of-two counts give codes of 1 to 16 bits (three LUT levels for
+    the longest); with the data drawn uniformly the oracle still restores the
+    original bytes."""
+    from ecf8_b200 import codec
+    from helpers import fp8_from_exponents, table_to_arrays
+    rng = np.random.default_rng(11)
+    table = codec.huffman_code_table({int(s): 1 << i for i, s in enumerate(rng.permutation(16))})
+    bits, vals, eb, ev = table_to_arrays(table)
+    assert bits.max() == 16
+    e = rng.integers(0, 16, 100000).astype(np.uint8)
+    enc, gaps, op = oracle_mod.encode(e, bits, vals, eb, ev)
+    fp8 = fp8_from_exponents(e, rng)
+    _, packed = oracle_mod.split(fp8)
+    s = {"luts": codec.get_luts_from_huffman_table(table).numpy(), "encoded": enc, "packed": packed,
+         "gaps": gaps, "output_positions": op}
+    out, _ = oracle_mod.decode(s)
+    assert np.array_equal(out, fp8)
