@@ -102,8 +102,8 @@ def test_dahuffman_standin_gives_complete_prefix_codes():
 
 
 def test_oracle_decodes_codes_up_to_16_bits(oracle_mod):
-    """Power-of-two counts give codes of 1 to 16 bits (three LUT levels for
-    the longest); with the data drawn uniformly the oracle still restores the
+    """Power-of-two counts give codes of 1 to 16 bits (the longest take both
+    LUT levels); with the data drawn uniformly the oracle still restores the
     original bytes."""
     from ecf8_b200 import codec
     from helpers import fp8_from_exponents, table_to_arrays
