@@ -18,7 +18,7 @@ ERR_CUDA = 3
 ERR_TOO_LARGE = 4
 NOALLOC_MAX_ELEMENTS = 268435456
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 TABLE_BYTES = 81920  # prepared decode table (ecf8_build_table)
 MAX_LUTS = 18
 MAX_BATCH = 128

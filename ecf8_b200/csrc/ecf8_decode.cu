@@ -24,7 +24,9 @@
 //    into the warp's output-ordered nibble buffer, whose partial last chunk
 //    carries into the next round.
 //  * Staging and merge.  Each round's bitstream and gaps are staged into
-//    shared memory with 16-byte cp.async one round ahead and its packed
+//    the warp's shared memory with 16-byte cp.async one round ahead (the
+//    copy starts once every lane holds its bytes of the current round in
+//    registers) and its packed
 //    sign+mantissa nibbles are loaded into registers during the decode;
 //    exponent and packed nibbles are merged 16 elements at a time with
 //    byte-permute/logic ops and written with one 16-byte store.
@@ -55,7 +57,7 @@ constexpr int kRoundGaps = 32;                          // gap bytes per round (
 constexpr int kTabBits = 13;                            // multi-symbol table width
 constexpr int kTabSize = 1 << kTabBits;
 constexpr int kMaxSymsPerEntry = 6;                     // 6 nibbles fit in bits 31..8
-constexpr int kSlotWords = 17;                          // 136 nibbles >= 128 + 4 overshoot (odd stride)
+constexpr int kSlotWords = 19;                          // 152 nibbles >= 127 + 12 overshoot (odd stride)
 constexpr int kMaxGroupElems = kGroupWindows * 64;      // one symbol per bit at most
 constexpr int kLutRows = ECF8_MAX_LUTS - 1;             // decode rows (row 0 + prefixes)
 constexpr int kGapStage = kGroupWindows / 2;            // gap bytes per group
@@ -70,8 +72,8 @@ constexpr int kObufWords = (2 * ((kRoundNibbles + 15) / 16) + 3) / 4 * 4;
 struct alignas(16) WarpBuf {
     uint32_t slot[32 * kSlotWords];  // per-lane decoded nibbles (MSB first)
     uint32_t obuf[kObufWords];       // output-ordered exponent nibbles of one round
-    uint8_t enc[2][kRoundStage];     // staged bitstream of a round, double buffered
-    uint8_t gaps[2][kRoundGaps];     // staged gaps of a round, double buffered
+    uint8_t enc[kRoundStage];        // staged bitstream of the next round
+    uint8_t gaps[kRoundGaps];        // staged gaps of the next round
 };
 static_assert(offsetof(WarpBuf, obuf) % 16 == 0, "obuf must allow 16-byte accesses");
 static_assert(offsetof(WarpBuf, enc) % 16 == 0 && kRoundStage % 16 == 0, "cp.async targets are 16-byte units");
@@ -145,11 +147,11 @@ __device__ __forceinline__ void cp_async16_full(uint32_t dst_s, const void* src)
 
 // ---------------------------------------------------------------------------
 // Per-stream set-up.  Entry layout (64 bits): x holds up to six 4-bit
-// symbols, first symbol in bits 31..28, and four times the symbol count in
-// bits 4..0 (directly a funnel-shift amount); y is the counter step (bits the
-// symbols use) << 24 | four times the count.  An all-zero entry means no
-// complete code starts the pattern within the 13 bits; the decoder then uses
-// the two-level LUT directly.
+// symbols, first symbol in bits 31..28, and the bits they use in bits 4..0
+// (directly a funnel-shift amount); y is the counter step: the bits << 23 |
+// four times the symbol count.  A pattern with no complete code within the
+// 13 bits gets the no-code step (x = 0); the decoder then uses the two-level
+// LUT directly.
 // ---------------------------------------------------------------------------
 template <class SM>
 __device__ __forceinline__ uint32_t lut_symbol(const SM& S, uint32_t top) {
@@ -235,14 +237,15 @@ __device__ void load_luts(SM& S, const DevStream& d) {
 
 // A table entry (64 bits): x = up to six 4-bit symbols, first in bits 31..28,
 // with the bits they use in bits 4..0 (the window's funnel-shift amount);
-// y = the counter step (bits << 24) | 4 x count (see decode_run), whose low
+// y = the counter step (bits << 23) | 4 x count (see decode_run), whose low
 // five bits are the accumulator's funnel-shift amount.  No complete code
 // within the table width: x = 0 and y = kNoCode, a step that only moves the
 // bit position past the end of any run, so the run loop exits to its
 // long-code path.
-constexpr uint32_t kNoCode = 0x80000000u;
+constexpr int kPosShift = 23;                          // counter bit position field: bits 31..23
+constexpr uint32_t kNoCode = 128u << kPosShift;
 __device__ __forceinline__ uint2 make_entry(uint32_t syms, uint32_t bits, uint32_t count) {
-    return count ? make_uint2(syms | bits, (bits << 24) | (4 * count)) : make_uint2(0u, kNoCode);
+    return count ? make_uint2(syms | bits, (bits << kPosShift) | (4 * count)) : make_uint2(0u, kNoCode);
 }
 
 // A prepared entry as read from memory, with every field the decode relies
@@ -250,7 +253,7 @@ __device__ __forceinline__ uint2 make_entry(uint32_t syms, uint32_t bits, uint32
 // so a table that ecf8_build_table did not write cannot stall a run or make
 // it emit more symbols than it has bits.
 __device__ __forceinline__ uint2 sanitize_entry(uint2 e) {
-    const uint32_t b = e.y >> 24, c4 = e.y & 31u;
+    const uint32_t b = e.y >> kPosShift, c4 = e.y & 31u;
     if (b == 0 || b > (uint32_t)kTabBits || c4 == 0 || (c4 & 3u) || c4 > 4u * kMaxSymsPerEntry || c4 > 4u * b)
         return make_uint2(0u, kNoCode);
     return make_entry(e.x & 0xffffff00u, b, c4 >> 2);
@@ -311,7 +314,7 @@ __device__ void derive_table(SM& S) {
 // of decode_run counts the entry's symbols that start before a bit offset).
 template <class SM>
 __device__ __forceinline__ uint16_t entry_start_mask(const SM& S, uint2 e) {
-    return e.x ? (uint16_t)(entry_ends(S, e) & ((1u << (e.y >> 24)) - 1u)) : (uint16_t)0;
+    return e.x ? (uint16_t)(entry_ends(S, e) & ((1u << (e.y >> kPosShift)) - 1u)) : (uint16_t)0;
 }
 
 __device__ void build_ends(Smem& S) {
@@ -349,12 +352,16 @@ __device__ void setup_stream(SM& S, const DevStream& d) {
 // [gap, 128) -- the two windows' counts of decode.cu:65-112 together.
 //
 // One counter K carries all of a step's bookkeeping: bits 4..0 are the
-// nibble bits of the open slot word, bits 23..5 that word's shared address / 4
-// (carries out of bit 4 advance it), bits 31..24 the bit position p.  A table
+// nibble bits of the open slot word, bits 22..5 that word's shared address / 4
+// (carries out of bit 4 advance it), bits 31..23 the bit position p.  A table
 // entry's y word is the counter step, so one add does it.  The slot store is
-// unconditional (a partly filled word is rewritten until it is full).  Codes
-// longer than the table width take the two-level LUT inside the loop, so that
-// a warp stays converged.
+// unconditional (a partly filled word is rewritten until it is full).  The
+// loop takes two table steps per iteration and checks the run's end once,
+// so its last iteration may run up to two steps past bit 128 (at most 12
+// nibbles past the 127 codes before it: the slot has room for 152).  A
+// no-code step moves p by 128 (two of them by 256, within the 9-bit field)
+// and so leaves the loop, whose exit takes the code from the two-level LUT and
+// re-enters; the loop body has no branch of its own.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void lds64(uint32_t a, uint32_t& lo, uint32_t& hi) {
     asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(lo), "=r"(hi) : "r"(a));
@@ -363,75 +370,101 @@ __device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
     asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
 }
 
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-    uint32_t v;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
-    return v;
-}
-
-// tail_s: shared address of the run's stream bytes 12..19 (bits 96..159).
+// w3, w4: the run's stream bytes 12..19 (bits 96..159), for the end fix-up.
 __device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, uint32_t w0, uint32_t w1,
-                                               uint32_t w2, uint32_t w3, uint32_t w4, uint32_t gap,
-                                               uint32_t tail_s) {
+                                               uint32_t w2, uint32_t w3, uint32_t w4, uint32_t gap) {
     const uint32_t tab_s = (uint32_t)__cvta_generic_to_shared(S.tab);
     uint32_t h = __funnelshift_l(w1, w0, gap);
     uint32_t m = __funnelshift_l(w2, w1, gap);
     uint32_t x = __funnelshift_l(w3, w2, gap);
     uint32_t y = __funnelshift_l(w4, w3, gap);
     uint32_t z = w4 << gap;
-    uint32_t K = (gap << 24) | ((slot_s >> 2) << 5);
-    uint32_t ah = 0, al = 0, elo, ehi;
+    uint32_t K = (gap << kPosShift) | ((slot_s >> 2) << 5);
+    uint32_t ah = 0, al = 0, elo1, ehi1, elo2, ehi2;
 #pragma unroll 1
     for (;;) {
+        // Two table steps per iteration: the second looks up the bits after
+        // the first's (h1), the register window then moves by both at once.
 #pragma unroll 1
         do {
-            const uint32_t sa = (K >> 3) & 0x1ffffcu;
-            lds64(tab_s + ((h >> (32 - kTabBits)) << 3), elo, ehi);
-            ah = __funnelshift_l(al, ah, ehi);  // append the entry's symbols; shift = ehi & 31 = 4 x count
-            al = __funnelshift_l(elo, al, ehi);
-            K += ehi;
-            sts32(sa, __funnelshift_r(al, ah, K));
-            h = __funnelshift_l(m, h, elo);  // consume the entry's bits; shift = elo & 31
-            m = __funnelshift_l(x, m, elo);
-            x = __funnelshift_l(y, x, elo);
-            y = __funnelshift_l(z, y, elo);
-            z = __funnelshift_l(0u, z, elo);
-        } while (K < (128u << 24));
-        if (__builtin_expect(ehi != kNoCode, 1)) break;
-        // No complete code within the table width (decode.cu:86-91): the
-        // no-code step left everything but the bit position alone.
-        K -= kNoCode;
+            lds64(tab_s + ((h >> (32 - kTabBits)) << 3), elo1, ehi1);
+            const uint32_t h1 = __funnelshift_l(m, h, elo1);
+            lds64(tab_s + ((h1 >> (32 - kTabBits)) << 3), elo2, ehi2);
+            const uint32_t sa1 = (K >> 3) & 0xffffcu;
+            ah = __funnelshift_l(al, ah, ehi1);  // append the entry's symbols; shift = ehi & 31 = 4 x count
+            al = __funnelshift_l(elo1, al, ehi1);
+            K += ehi1;
+            sts32(sa1, __funnelshift_r(al, ah, K));
+            const uint32_t sa2 = (K >> 3) & 0xffffcu;
+            ah = __funnelshift_l(al, ah, ehi2);
+            al = __funnelshift_l(elo2, al, ehi2);
+            K += ehi2;
+            sts32(sa2, __funnelshift_r(al, ah, K));
+            const uint32_t b = elo1 + elo2;  // low five bits: both steps' bits (at most 26)
+            h = __funnelshift_l(m, h, b);
+            m = __funnelshift_l(x, m, b);
+            x = __funnelshift_l(y, x, b);
+            y = __funnelshift_l(z, y, b);
+            z = __funnelshift_l(0u, z, b);
+        } while (K < (128u << kPosShift));
+        if (__builtin_expect(ehi2 != kNoCode, 1)) break;
+        // A no-code step (decode.cu:86-91).  If the first step was one, the
+        // second read the same bits and was one too; either left everything
+        // but the bit position alone.
+        if (ehi1 == kNoCode) {
+            K -= 2 * kNoCode;
+        } else {
+            K -= kNoCode;
+            if (K >= (128u << kPosShift)) {  // the first step already reached the run's end
+                elo2 = ehi2 = 0u;
+                break;
+            }
+        }
         const uint32_t sym = lut_symbol(S, h);
         const uint32_t len = min(code_length(S, sym), 31u);
-        elo = ((sym & 15u) << 28) | len;
-        ehi = (len << 24) | 4u;
-        const uint32_t sa = (K >> 3) & 0x1ffffcu;
-        ah = __funnelshift_l(al, ah, ehi);
-        al = __funnelshift_l(elo, al, ehi);
-        K += ehi;
+        elo1 = ((sym & 15u) << 28) | len;
+        ehi1 = (len << kPosShift) | 4u;
+        elo2 = ehi2 = 0u;
+        const uint32_t sa = (K >> 3) & 0xffffcu;
+        ah = __funnelshift_l(al, ah, ehi1);
+        al = __funnelshift_l(elo1, al, ehi1);
+        K += ehi1;
         sts32(sa, __funnelshift_r(al, ah, K));
-        h = __funnelshift_l(m, h, elo);
-        m = __funnelshift_l(x, m, elo);
-        x = __funnelshift_l(y, x, elo);
-        y = __funnelshift_l(z, y, elo);
-        z = __funnelshift_l(0u, z, elo);
-        if (K >= (128u << 24)) break;
+        h = __funnelshift_l(m, h, elo1);
+        m = __funnelshift_l(x, m, elo1);
+        x = __funnelshift_l(y, x, elo1);
+        y = __funnelshift_l(z, y, elo1);
+        z = __funnelshift_l(0u, z, elo1);
+        if (K >= (128u << kPosShift)) break;
     }
     const uint32_t m4 = K & 31u;
-    const uint32_t words = ((K >> 5) & 0x7ffffu) - (slot_s >> 2);
+    const uint32_t words = ((K >> 5) & 0x3ffffu) - (slot_s >> 2);
     if (m4) sts32(slot_s + 4 * words, al << (32 - m4));
     uint32_t n = words * 8 + (m4 >> 2);
-    // The last step may have taken codes that start at or after the run's
-    // end; they belong to the next run.  The step started at bit 128 - room >
-    // 96; its entry's end offsets tell how many codes start before the end.
-    const uint32_t room = 128u - ((K >> 24) - (ehi >> 24));
-    if (room < (uint32_t)kTabBits) {
-        const uint32_t b3 = __byte_perm(lds32(tail_s), 0, 0x0123), b4 = __byte_perm(lds32(tail_s + 4), 0, 0x0123);
-        const uint32_t idx = __funnelshift_l(b4, b3, 32u - room) >> (32 - kTabBits);
-        const uint32_t c = (ehi & 31u) >> 2;
-        const uint32_t keep = min(1u + __popc(S.ends[idx] & ((1u << room) - 1u)), c);
-        n -= c - keep;
+    // The last iteration may have taken codes that start at or after the
+    // run's end; they belong to the next run.  Its second step started at p1,
+    // its first at p0.  If p1 >= 128 the second step's codes all go and the
+    // first step's entry end offsets tell how many of its codes start before
+    // the end; otherwise the second step's do.
+    const uint32_t p1 = (K >> kPosShift) - (ehi2 >> kPosShift);
+    const uint32_t c1 = (ehi1 & 31u) >> 2, c2 = (ehi2 & 31u) >> 2;
+    uint32_t q, c, drop;
+    if (p1 >= 128u) {
+        q = p1 - (ehi1 >> kPosShift);
+        c = c1;
+        drop = c2;
+    } else {
+        q = p1;
+        c = c2;
+        drop = 0u;
     }
+    const uint32_t room = 128u - q;
+    if (room < (uint32_t)kTabBits) {
+        const uint32_t idx = __funnelshift_l(w4, w3, 32u - room) >> (32 - kTabBits);
+        const uint32_t keep = min(1u + __popc(S.ends[idx] & ((1u << room) - 1u)), c);
+        drop += c - keep;
+    }
+    n -= min(drop, n);
     return min(n, 128u - gap);  // codes start at distinct bits of [gap, 128); binds only for a corrupt table
 }
 
@@ -521,9 +554,9 @@ __device__ __forceinline__ void place_run(uint32_t* obuf, const uint32_t* slot, 
 // past the end of the stream.  cp.async when the stream's buffers are 16-byte
 // aligned, plain loads otherwise.  The lanes read each other's bytes only
 // after the warp's next __syncwarp.
-__device__ __forceinline__ void stage_round(WarpBuf& W, const DevStream& d, int b, int g, int r, int lane) {
+__device__ __forceinline__ void stage_round(WarpBuf& W, const DevStream& d, int g, int r, int lane) {
     const long long lo = (long long)g * kGroupBytes + (long long)r * kRoundBytes;
-    const uint32_t eb = (uint32_t)__cvta_generic_to_shared(W.enc[b]);
+    const uint32_t eb = (uint32_t)__cvta_generic_to_shared(W.enc);
     if (d.async_ok && lo + kRoundStage <= d.n_bytes) {
         cp_async16_full(eb + 16 * lane, d.encoded + lo + 16 * lane);
         if (lane == 0) cp_async16_full(eb + kRoundBytes, d.encoded + lo + kRoundBytes);
@@ -532,19 +565,19 @@ __device__ __forceinline__ void stage_round(WarpBuf& W, const DevStream& d, int 
         for (int i = 16 * lane; i < kRoundStage; i += 32 * 16) {
             const int v = (int)min(max(vl - i, 0ll), 16ll);  // bytes of this unit inside the stream
             if (d.async_ok) {
-                cp_async16(W.enc[b] + i, v ? d.encoded + lo + i : d.encoded, (uint32_t)v);
+                cp_async16(W.enc + i, v ? d.encoded + lo + i : d.encoded, (uint32_t)v);
             } else {
 #pragma unroll
-                for (int k = 0; k < 16; ++k) W.enc[b][i + k] = k < v ? __ldg(d.encoded + lo + i + k) : (uint8_t)0;
+                for (int k = 0; k < 16; ++k) W.enc[i + k] = k < v ? __ldg(d.encoded + lo + i + k) : (uint8_t)0;
             }
         }
     }
     const long long glo = (long long)g * kGapStage + (long long)r * kRoundGaps;  // gaps exist for every group
     if (d.async_ok) {
         if (lane < kRoundGaps / 16)
-            cp_async16_full((uint32_t)__cvta_generic_to_shared(W.gaps[b]) + 16 * lane, d.gaps + glo + 16 * lane);
+            cp_async16_full((uint32_t)__cvta_generic_to_shared(W.gaps) + 16 * lane, d.gaps + glo + 16 * lane);
     } else {
-        W.gaps[b][lane] = __ldg(d.gaps + glo + lane);
+        W.gaps[lane] = __ldg(d.gaps + glo + lane);
     }
 }
 
@@ -639,6 +672,11 @@ __device__ __forceinline__ void flush_group(WarpBuf& W, const DevStream& d, unsi
     }
 }
 
+// Stream bytes from round r of group g on.
+__device__ __forceinline__ long long rem_of(long long n_bytes, int g, int r) {
+    return n_bytes - (long long)g * kGroupBytes - (long long)r * kRoundBytes;
+}
+
 // One warp decodes groups g0, g0 + kWarps, ... below g_end of stream d, each
 // in eight rounds of 64 windows: lane i decodes windows 2i and 2i + 1 of the
 // round as one run into its slot, a warp-shuffle scan places the runs, and
@@ -652,7 +690,6 @@ __device__ __forceinline__ void flush_group(WarpBuf& W, const DevStream& d, unsi
 __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int g0, int g_end, int lane) {
     uint32_t* slot = W.slot + lane * kSlotWords;
     const uint32_t slot_s = (uint32_t)__cvta_generic_to_shared(slot);
-    const uint32_t enc_s0 = (uint32_t)__cvta_generic_to_shared(W.enc[0]);
     const long long n_bytes = d.n_bytes;
     const bool fast = d.out16 && d.async_ok;
     // The first round's bytes and the first group's range are fetched while
@@ -660,7 +697,7 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int g0, int
     GroupRange rg{0, 0};
     if (g0 < g_end) {
         for (int i = lane; i < kObufWords / 4; i += 32) reinterpret_cast<uint4*>(W.obuf)[i] = make_uint4(0, 0, 0, 0);
-        stage_round(W, d, 0, g0, 0, lane);
+        stage_round(W, d, g0, 0, lane);
         rg = group_range(d, g0);
     }
     cp_async_commit();
@@ -669,7 +706,7 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int g0, int
     cp_async_wait<0>();
     __syncwarp();
 
-    int g = g0, r = 0, buf = 0;
+    int g = g0, r = 0;
     unsigned long long base = rg.start & ~15ull;
     uint32_t rs = (uint32_t)(rg.start - base), re = (uint32_t)(rg.end - base), P = rs;
     GroupRange rn = g + kWarps < g_end ? group_range(d, g + kWarps) : GroupRange{0, 0};
@@ -678,24 +715,28 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int g0, int
 #pragma unroll 1
     for (;;) {
         const bool last_round = r == kRounds - 1;
+        // This lane's window pair of the staged round; then the buffer takes the next round.
+        const bool active = rem_of(n_bytes, g, r) > 16 * lane;
+        uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+        uint32_t r4 = 0u, gap = 0u;
+        if (active) {
+            raw = *reinterpret_cast<const uint4*>(W.enc + 16 * lane);
+            r4 = *reinterpret_cast<const uint32_t*>(W.enc + 16 * lane + 16);
+            gap = W.gaps[lane] >> 4;
+        }
+        __syncwarp();
         if (!last_round)
-            stage_round(W, d, buf ^ 1, g, r + 1, lane);
+            stage_round(W, d, g, r + 1, lane);
         else if (g + kWarps < g_end)
-            stage_round(W, d, buf ^ 1, g + kWarps, 0, lane);
+            stage_round(W, d, g + kWarps, 0, lane);
         cp_async_commit();
 
         // --- decode this lane's window pair ---
         uint32_t count = 0;
-        const long long rem = n_bytes - (long long)g * kGroupBytes - (long long)r * kRoundBytes;
-        if (rem > 16 * lane) {
-            const uint8_t* e = W.enc[buf] + 16 * lane;
-            const uint4 raw = *reinterpret_cast<const uint4*>(e);
-            const uint32_t r4 = *reinterpret_cast<const uint32_t*>(e + 16);
+        if (active)
             count = decode_run(S, slot_s, __byte_perm(raw.x, 0, 0x0123), __byte_perm(raw.y, 0, 0x0123),
                                __byte_perm(raw.z, 0, 0x0123), __byte_perm(raw.w, 0, 0x0123),
-                               __byte_perm(r4, 0, 0x0123), W.gaps[buf][lane] >> 4,
-                               enc_s0 + buf * kRoundStage + 16 * lane + 12);
-        }
+                               __byte_perm(r4, 0, 0x0123), gap);
         // A pair wholly past n_bytes only follows the last real code: it places nothing.
 
         // --- exclusive scan of run counts (decode.cu:114-148) ---
@@ -717,7 +758,6 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int g0, int
         cp_async_wait<0>();  // this lane's copies of the next round
         __syncwarp();
         P = Pn;
-        buf ^= 1;
         if (!last_round) {
             ++r;
             if (fast) prefetch_packed(pw, d, base, Cn, re, lane);

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ECF8_ABI_VERSION 4
+#define ECF8_ABI_VERSION 5
 
 /* Status codes. */
 #define ECF8_OK 0
