@@ -344,7 +344,7 @@ def test_corrupt_prepared_table_stays_in_bounds(cuda_device):
             b = rng.integers(1, 14, 8192).astype(np.uint32)
             c = rng.integers(1, 7, 8192).astype(np.uint32)
             ent[:, 0] = (ent[:, 0] & 0xffffff00) | b
-            ent[:, 1] = (b << 24) | (4 * c)
+            ent[:, 1] = (b << 23) | (4 * c)
         table = torch.from_numpy(t.view(np.int32).copy()).to(cuda_device)
         buf = torch.full((n + 64,), GUARD, dtype=torch.uint8, device=cuda_device)
         decode_stream(d["luts"], d["encoded"], d["packed_other_4bits"], d["output_positions"], d["gaps"],
