@@ -18,10 +18,11 @@ ERR_CUDA = 3
 ERR_TOO_LARGE = 4
 NOALLOC_MAX_ELEMENTS = 268435456
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 TABLE_BYTES = 81920  # prepared decode table (ecf8_build_table)
 MAX_LUTS = 18
 MAX_BATCH = 128
+DECODE_OVERLAP_PREVIOUS = 1  # ecf8_decode_batch_flags: may start while the stream's previous kernel runs
 THREADS_PER_BLOCK = 512
 BYTES_PER_THREAD = 8
 
@@ -56,6 +57,8 @@ SIGNATURES = {
     "ecf8_build_table": (ctypes.c_int, [_c_u8p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     "ecf8_decode_batch": (ctypes.c_int, [ctypes.POINTER(Ecf8Stream), ctypes.c_int, ctypes.c_int,
                                          ctypes.c_int, ctypes.c_void_p]),
+    "ecf8_decode_batch_flags": (ctypes.c_int, [ctypes.POINTER(Ecf8Stream), ctypes.c_int, ctypes.c_int,
+                                               ctypes.c_int, ctypes.c_uint32, ctypes.c_void_p]),
     "ecf8_encode_workspace_bytes": (ctypes.c_int64, [_i64]),
     "ecf8_encode_plan": (ctypes.c_int, [_c_u8p, _i64, ctypes.c_char_p, ctypes.c_int, ctypes.c_void_p,
                                         ctypes.c_void_p]),

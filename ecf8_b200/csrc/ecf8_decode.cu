@@ -702,6 +702,11 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int g0, int
     }
     cp_async_commit();
     setup_stream(S, d);
+    // Under programmatic dependent launch (ECF8_DECODE_OVERLAP_PREVIOUS) the
+    // set-up above may run while the stream's previous kernel finishes; the
+    // outputs are written only after it has completed.  Without that launch
+    // attribute this returns at once.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if (g0 >= g_end) return;
     cp_async_wait<0>();
     __syncwarp();
@@ -779,6 +784,10 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int g0, int
 
 template <int MAXS>
 __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ Batch<MAXS> B) {
+    // A decode launched next with ECF8_DECODE_OVERLAP_PREVIOUS may start its
+    // set-up on the SMs this grid leaves; it writes nothing before this grid
+    // has completed.
+    asm volatile("griddepcontrol.launch_dependents;");
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem& S = *reinterpret_cast<Smem*>(smem_raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -905,8 +914,14 @@ int make_stream(const ecf8_stream& s, DevStream* d) {
     return ECF8_OK;
 }
 
+int check_format(int threads_per_block, int bytes_per_thread) {
+    if (threads_per_block != ECF8_THREADS_PER_BLOCK || bytes_per_thread != ECF8_BYTES_PER_THREAD)
+        return ECF8_ERR_UNSUPPORTED;
+    return ECF8_OK;
+}
+
 template <int MAXS>
-int launch(const ecf8_stream* streams, int n, cudaStream_t stream) {
+int launch(const ecf8_stream* streams, int n, cudaStream_t stream, bool overlap) {
     Batch<MAXS> B;
     long long total = 0;
     int m = 0;
@@ -928,17 +943,48 @@ int launch(const ecf8_stream* streams, int n, cudaStream_t stream) {
     if (st != ECF8_OK) return st;
     long long grid = (long long)info.sms * info.blocks_per_sm;
     if (grid > total) grid = total;
-    decode_kernel<MAXS><<<(unsigned)grid, kThreads, sizeof(Smem), stream>>>(B);
-    cudaError_t e = cudaGetLastError();
+    if (!overlap) {
+        decode_kernel<MAXS><<<(unsigned)grid, kThreads, sizeof(Smem), stream>>>(B);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return cuda_fail(e);
+        return ECF8_OK;
+    }
+    // Programmatic dependent launch: the grid may begin once the previous
+    // kernel on the stream has let dependents start (or has finished).
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = sizeof(Smem);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, decode_kernel<MAXS>, B);
     if (e != cudaSuccess) return cuda_fail(e);
     return ECF8_OK;
 }
 
-int check_format(int threads_per_block, int bytes_per_thread) {
-    if (threads_per_block != ECF8_THREADS_PER_BLOCK || bytes_per_thread != ECF8_BYTES_PER_THREAD)
-        return ECF8_ERR_UNSUPPORTED;
+int decode_batch(const ecf8_stream* streams, int n_streams, int threads_per_block, int bytes_per_thread,
+                 bool overlap, void* cuda_stream) {
+    int st = check_format(threads_per_block, bytes_per_thread);
+    if (st != ECF8_OK) return st;
+    if (n_streams < 0 || (n_streams > 0 && !streams)) return ECF8_ERR_INVALID_ARGUMENT;
+    // Validate everything before launching anything.
+    for (int i = 0; i < n_streams; ++i) {
+        DevStream d;
+        st = make_stream(streams[i], &d);
+        if (st != ECF8_OK) return st;
+    }
+    for (int i = 0; i < n_streams; i += ECF8_MAX_BATCH) {
+        const int n = n_streams - i < ECF8_MAX_BATCH ? n_streams - i : ECF8_MAX_BATCH;
+        st = launch<ECF8_MAX_BATCH>(streams + i, n, (cudaStream_t)cuda_stream, overlap);
+        if (st != ECF8_OK) return st;
+    }
     return ECF8_OK;
 }
+
 
 }  // namespace
 }  // namespace ecf8
@@ -965,26 +1011,19 @@ int ecf8_decode(const uint8_t* luts, const uint8_t* encoded, const uint8_t* pack
     s.outputs = outputs;
     s.n_elements = n_elements;
     s.table = nullptr;
-    return ecf8::launch<1>(&s, 1, (cudaStream_t)cuda_stream);
+    return ecf8::launch<1>(&s, 1, (cudaStream_t)cuda_stream, false);
 }
 
 int ecf8_decode_batch(const ecf8_stream* streams, int n_streams, int threads_per_block,
                       int bytes_per_thread, void* cuda_stream) {
-    int st = ecf8::check_format(threads_per_block, bytes_per_thread);
-    if (st != ECF8_OK) return st;
-    if (n_streams < 0 || (n_streams > 0 && !streams)) return ECF8_ERR_INVALID_ARGUMENT;
-    // Validate everything before launching anything.
-    for (int i = 0; i < n_streams; ++i) {
-        ecf8::DevStream d;
-        st = ecf8::make_stream(streams[i], &d);
-        if (st != ECF8_OK) return st;
-    }
-    for (int i = 0; i < n_streams; i += ECF8_MAX_BATCH) {
-        const int n = n_streams - i < ECF8_MAX_BATCH ? n_streams - i : ECF8_MAX_BATCH;
-        st = ecf8::launch<ECF8_MAX_BATCH>(streams + i, n, (cudaStream_t)cuda_stream);
-        if (st != ECF8_OK) return st;
-    }
-    return ECF8_OK;
+    return ecf8::decode_batch(streams, n_streams, threads_per_block, bytes_per_thread, false, cuda_stream);
+}
+
+int ecf8_decode_batch_flags(const ecf8_stream* streams, int n_streams, int threads_per_block,
+                            int bytes_per_thread, uint32_t flags, void* cuda_stream) {
+    if (flags & ~(uint32_t)ECF8_DECODE_OVERLAP_PREVIOUS) return ECF8_ERR_INVALID_ARGUMENT;
+    return ecf8::decode_batch(streams, n_streams, threads_per_block, bytes_per_thread,
+                              (flags & ECF8_DECODE_OVERLAP_PREVIOUS) != 0, cuda_stream);
 }
 
 int ecf8_build_table(const uint8_t* luts, int n_luts, uint32_t* table, void* cuda_stream) {

@@ -129,13 +129,17 @@ def _check_stream(s, out, device, table=None):
 
 
 def decode_stream(luts, encoded, packed_other_4bits, output_positions, gaps, out=None,
-                  threads_per_block=512, bytes_per_thread=8, stream=None, table=None):
+                  threads_per_block=512, bytes_per_thread=8, stream=None, table=None, overlap_previous=False):
     """Decodes one ECF8 stream (the five buffers a compressed block holds) into
     `out` (e4m3 or uint8, n = 2 * packed_other_4bits.numel() elements;
     allocated if None).  `table` is the stream's prepared decode table
     (build_decode_table), or None to derive it inside the kernel.
     Asynchronous on `stream` (default: the current stream of the buffers'
-    device).  Returns `out`."""
+    device).  With overlap_previous=True the launch may start while the
+    stream's previous kernel runs and writes `out` only after it has finished
+    (ECF8_DECODE_OVERLAP_PREVIOUS); the caller guarantees that no work still
+    in flight on the stream writes the stream buffers or the table.  Returns
+    `out`."""
     device = encoded.device
     if device.type != "cuda":
         raise ValueError("ECF8 decode runs on a CUDA device; move the stream buffers there first")
@@ -148,7 +152,11 @@ def decode_stream(luts, encoded, packed_other_4bits, output_positions, gaps, out
     L = _lib.lib()
     with torch.cuda.device(device):
         cs = stream if stream is not None else torch.cuda.current_stream(device)
-        if table is None:
+        if overlap_previous:
+            arr = (_lib.Ecf8Stream * 1)(_stream_struct(s, out, table))
+            st = L.ecf8_decode_batch_flags(arr, 1, threads_per_block, bytes_per_thread,
+                                           _lib.DECODE_OVERLAP_PREVIOUS, cs.cuda_stream)
+        elif table is None:
             st = L.ecf8_decode(luts.data_ptr(), encoded.data_ptr(), packed_other_4bits.data_ptr(),
                                output_positions.data_ptr(), gaps.data_ptr(), out.data_ptr(),
                                luts.shape[0], encoded.numel(), n,
@@ -162,10 +170,12 @@ def decode_stream(luts, encoded, packed_other_4bits, output_positions, gaps, out
     return out
 
 
-def decode_streams(streams, outs, threads_per_block=512, bytes_per_thread=8, stream=None):
+def decode_streams(streams, outs, threads_per_block=512, bytes_per_thread=8, stream=None,
+                   overlap_previous=False):
     """Decodes several streams with one persistent launch per 128 streams.
     `streams` is a list of dicts with the five stream buffers (and optionally
-    "decode_table"); `outs` the matching output tensors.  All on one device."""
+    "decode_table"); `outs` the matching output tensors.  All on one device.
+    overlap_previous as in decode_stream."""
     if len(streams) != len(outs):
         raise ValueError("one output per stream")
     if not streams:
@@ -179,8 +189,9 @@ def decode_streams(streams, outs, threads_per_block=512, bytes_per_thread=8, str
     L = _lib.lib()
     with torch.cuda.device(device):
         cs = stream if stream is not None else torch.cuda.current_stream(device)
-        st = L.ecf8_decode_batch(arr, len(streams), threads_per_block, bytes_per_thread, cs.cuda_stream)
-    _lib.check(st, "ecf8_decode_batch")
+        flags = _lib.DECODE_OVERLAP_PREVIOUS if overlap_previous else 0
+        st = L.ecf8_decode_batch_flags(arr, len(streams), threads_per_block, bytes_per_thread, flags, cs.cuda_stream)
+    _lib.check(st, "ecf8_decode_batch_flags")
     return outs
 
 
@@ -260,11 +271,17 @@ def get_hook(threads_per_block, bytes_per_thread):
         # decode on a device and kept as a non-persistent buffer (it is not
         # part of the checkpoint).
         table = getattr(module, "ecf8_decode_table", None)
-        if table is None or table.device != device:
+        fresh = table is None or table.device != device
+        if fresh:
             table = build_decode_table(module.luts)
             module.register_buffer("ecf8_decode_table", table, persistent=False)
+        # The block's buffers and an existing table are written only at load
+        # time, so the decode may start while the previous layer's last
+        # kernel runs (it overwrites the shared scratch only after that
+        # kernel); right after building the table it may not.
         decode_stream(module.luts, module.encoded, module.packed_other_4bits, module.output_positions,
-                      module.gaps, reconstructed, threads_per_block, bytes_per_thread, table=table)
+                      module.gaps, reconstructed, threads_per_block, bytes_per_thread, table=table,
+                      overlap_previous=not fresh)
         inject_weights(module, reconstructed)
 
     return decode_hook

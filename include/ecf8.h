@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ECF8_ABI_VERSION 5
+#define ECF8_ABI_VERSION 6
 
 /* Status codes. */
 #define ECF8_OK 0
@@ -115,6 +115,27 @@ int ecf8_build_table(const uint8_t* luts, int n_luts, uint32_t* table,
 int ecf8_decode_batch(const ecf8_stream* streams, int n_streams,
                       int threads_per_block, int bytes_per_thread,
                       void* cuda_stream);
+
+/*
+ * ecf8_decode_batch with flags.  flags = 0 behaves exactly like
+ * ecf8_decode_batch; other bits than the ones below are rejected
+ * (ECF8_ERR_INVALID_ARGUMENT).
+ *
+ * ECF8_DECODE_OVERLAP_PREVIOUS: launches with programmatic dependent launch.
+ * The decode may start while the previous kernel on cuda_stream is still
+ * running: it reads its inputs (luts, encoded, packed_other_4bits,
+ * output_positions, gaps, table) and builds its tables at once, and writes
+ * its outputs only after that kernel has completed.  Back-to-back decodes
+ * (one per layer) then overlap one launch's set-up with the previous one's
+ * last groups.  The caller guarantees that no work still in flight on the
+ * stream writes the inputs; work writing or reading the outputs is ordered
+ * as without the flag.  Has no counterpart in the reference (whose launches
+ * are plain stream-ordered kernels).
+ */
+#define ECF8_DECODE_OVERLAP_PREVIOUS 1u
+int ecf8_decode_batch_flags(const ecf8_stream* streams, int n_streams,
+                            int threads_per_block, int bytes_per_thread,
+                            uint32_t flags, void* cuda_stream);
 
 /*
  * GPU encoder, producing byte-identical buffers to the reference stream packer

@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.ecf8_abi_version() == 5
+    assert lib.ecf8_abi_version() == 6
     assert lib.ecf8_status_string(0) == b"ok"
     assert b"invalid" in lib.ecf8_status_string(1)
     assert lib.ecf8_last_cuda_error() == 0
@@ -97,3 +97,12 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(L, "library_path", lambda: str(tmp_path / "nope.so"))
     with pytest.raises(RuntimeError, match="no fallback"):
         L.lib()
+
+
+def test_decode_batch_flags_rejects_unknown_flags(lib):
+    """Unknown flag bits are refused before anything touches a device."""
+    from ecf8_b200 import _lib
+    assert lib.ecf8_decode_batch_flags(None, 0, 512, 8, 2, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.ecf8_decode_batch_flags(None, 0, 512, 8, 0x80000000, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.ecf8_decode_batch_flags(None, 0, 256, 8, _lib.DECODE_OVERLAP_PREVIOUS, None) == _lib.ERR_UNSUPPORTED
+    assert lib.ecf8_decode_batch_flags(None, 0, 512, 8, _lib.DECODE_OVERLAP_PREVIOUS, None) == _lib.OK

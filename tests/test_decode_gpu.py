@@ -352,3 +352,44 @@ def test_corrupt_prepared_table_stays_in_bounds(cuda_device):
         torch.cuda.synchronize()
         b = buf.cpu().numpy()
         assert np.all(b[:32] == GUARD) and np.all(b[32 + n:] == GUARD)
+
+
+def test_overlap_previous_back_to_back(cuda_device):
+    """ECF8_DECODE_OVERLAP_PREVIOUS: decodes that may start while the previous
+    kernel runs, one after another into one buffer (the hook's shared
+    scratch), each right after a kernel that writes that buffer, give the same
+    bytes as plain decodes; with and without prepared tables."""
+    from ecf8_b200.run import build_decode_table, decode_stream
+    names = golden_names()
+    ss = [load_golden(n) for n in names]
+    ds = [to_device(s, cuda_device) for s in ss]
+    tables = [build_decode_table(d["luts"]) for d in ds]
+    torch.cuda.synchronize()
+    n_max = max(s["fp8"].size for s in ss)
+    buf = torch.full((n_max + 64,), GUARD, dtype=torch.uint8, device=cuda_device)
+    for rep in range(2):
+        for s, d, t in zip(ss, ds, tables):
+            n = s["fp8"].size
+            out = buf[32:32 + n]
+            out.fill_(0x5A)  # the previous kernel writes the output region
+            decode_stream(d["luts"], d["encoded"], d["packed_other_4bits"], d["output_positions"], d["gaps"],
+                          out, table=t if rep == 0 else None, overlap_previous=True)
+            b = buf.cpu().numpy()
+            assert np.array_equal(b[32:32 + n], s["fp8"])
+            assert np.all(b[:32] == GUARD) and np.all(b[32 + n_max:] == GUARD)
+
+
+def test_overlap_previous_batched_matches_plain(cuda_device):
+    from ecf8_b200.run import build_decode_table, decode_streams
+    ss = [load_golden(n) for n in golden_names()]
+    ds = [to_device(s, cuda_device) for s in ss]
+    for d in ds:
+        d["decode_table"] = build_decode_table(d["luts"])
+    torch.cuda.synchronize()
+    for _ in range(3):
+        outs = [torch.zeros(s["fp8"].size, dtype=torch.uint8, device=cuda_device) for s in ss]
+        decode_streams(ds, outs, overlap_previous=True)
+        decode_streams(ds, outs, overlap_previous=True)
+        torch.cuda.synchronize()
+        for s, o in zip(ss, outs):
+            assert np.array_equal(o.cpu().numpy(), s["fp8"])
