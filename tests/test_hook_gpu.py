@@ -96,6 +96,10 @@ def test_hooked_model_matches_uncompressed(cuda_device, tmp_path, parallel):
     y = model(x)
     torch.cuda.synchronize()
     assert torch.equal(y, y_ref)
+    # Later forwards decode with the tables built on the first one, each
+    # launch overlapping the previous kernel (ECF8_DECODE_OVERLAP_PREVIOUS).
+    for _ in range(3):
+        assert torch.equal(model(x), y_ref)
     # every block decoded into the same per-device scratch
     ptrs = {blk.down_proj.weight.data_ptr() for blk in model.layers}
     assert len(ptrs) == 1
