@@ -19,17 +19,22 @@
 //    prepared table each CTA derives it itself.
 //  * Two windows per lane, one decode pass.  Each lane decodes its two
 //    adjacent 64-bit windows of the round as one continuous run (the first
-//    window's gap gives the start) into a private shared-memory slot of
-//    nibbles; a warp-shuffle scan places each run; slots are funnel-shifted
-//    into the warp's output-ordered nibble buffer, whose partial last chunk
-//    carries into the next round.
+//    window's gap gives the start), two table steps per loop iteration,
+//    into a private shared-memory slot of nibbles; a warp-shuffle scan
+//    places each run; slots are funnel-shifted into the warp's
+//    output-ordered nibble buffer, whose partial last chunk carries into
+//    the next round.
 //  * Staging and merge.  Each round's bitstream and gaps are staged into
 //    the warp's shared memory with 16-byte cp.async one round ahead (the
 //    copy starts once every lane holds its bytes of the current round in
-//    registers) and its packed
-//    sign+mantissa nibbles are loaded into registers during the decode;
-//    exponent and packed nibbles are merged 16 elements at a time with
-//    byte-permute/logic ops and written with one 16-byte store.
+//    registers) and its packed sign+mantissa nibbles are loaded into
+//    registers during the decode; exponent and packed nibbles are merged 16
+//    elements at a time with byte-permute/logic ops and written with one
+//    16-byte store.
+//  * Launch overlap (opt-in, ECF8_DECODE_OVERLAP_PREVIOUS).  With
+//    programmatic dependent launch a decode builds its tables and stages its
+//    first round while the stream's previous kernel finishes, and writes
+//    outputs only after that kernel has completed (griddepcontrol).
 //
 // No inter-CTA communication, no global scratch, no allocation, no spin-waits.
 
