@@ -139,13 +139,18 @@ def test_batch_of_all_golden_streams(cuda_device):
         assert np.array_equal(o.cpu().numpy(), s["fp8"]), n
 
 
-def test_batch_larger_than_one_launch(cuda_device, oracle_mod):
+@pytest.mark.parametrize("overlap", [False, True])
+def test_batch_larger_than_one_launch(cuda_device, oracle_mod, overlap):
+    """300 streams: three launches per call; with overlap each may start while
+    the one before it runs (their outputs are disjoint, their inputs were
+    written before the call)."""
     from ecf8_b200.run import decode_streams
     rng = np.random.default_rng(7)
     ss = [random_stream(oracle_mod, rng, n=int(rng.integers(1, 3000)) * 2) for _ in range(300)]
     ds = [to_device(s, cuda_device) for s in ss]
     outs = [torch.zeros(s["fp8"].size, dtype=torch.uint8, device=cuda_device) for s in ss]
-    decode_streams(ds, outs)
+    torch.cuda.synchronize()
+    decode_streams(ds, outs, overlap_previous=overlap)
     torch.cuda.synchronize()
     for s, o in zip(ss, outs):
         assert np.array_equal(o.cpu().numpy(), s["fp8"])
