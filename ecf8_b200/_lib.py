@@ -18,8 +18,8 @@ ERR_CUDA = 3
 ERR_TOO_LARGE = 4
 NOALLOC_MAX_ELEMENTS = 268435456
 
-ABI_VERSION = 6
-TABLE_BYTES = 81920  # prepared decode table (ecf8_build_table)
+ABI_VERSION = 7
+TABLE_BYTES = 86544  # prepared decode table (ecf8_build_table)
 MAX_LUTS = 18
 MAX_BATCH = 128
 DECODE_OVERLAP_PREVIOUS = 1  # ecf8_decode_batch_flags: may start while the stream's previous kernel runs

@@ -5,34 +5,37 @@
 // like the reference kernel dfloat/run/decode.cu:16-211, with a different
 // design:
 //
-//  * Persistent CTAs of independent warps.  One CTA of 27 warps per SM holds
-//    one copy of the stream's decode tables in shared memory; each warp
-//    decodes every 27th 4096-byte group (one reference thread block's worth
-//    of stream) of the CTA's range by itself, in eight rounds of 64 windows,
-//    so warps never wait for one another inside a stream.
+//  * Persistent CTAs of independent warps.  One CTA per SM holds one copy of
+//    the stream's decode tables in shared memory; each warp decodes its own
+//    contiguous run of 4096-byte groups (one reference thread block's worth
+//    of stream each), in rounds of 64 windows, so warps never wait for one
+//    another inside a stream.  Consecutive groups of a warp are consecutive
+//    in the output, so a warp's output buffer flows from group to group and
+//    only the first and last chunk of its range are written byte by byte.
 //  * Multi-symbol table.  An 8192-entry table indexed by the next 13 stream
 //    bits yields up to six whole symbols, the bits they use and their count,
 //    plus a counter step that advances the bit position, the output nibble
-//    count and the output word address with one add.  It is a pure function
-//    of the stream's LUTs: ecf8_build_table() derives it once per stream (at
-//    load time) and every CTA copies it into shared memory; without a
-//    prepared table each CTA derives it itself.
+//    count and the output word index with one add.  It is a pure function of
+//    the stream's LUTs: ecf8_build_table() derives it once per stream (at
+//    load time) and stores a copy of the LUTs with it; every CTA checks that
+//    copy against the stream's LUTs and copies the table into shared memory,
+//    or derives the table itself when there is none or it does not match.
 //  * Two windows per lane, one decode pass.  Each lane decodes its two
 //    adjacent 64-bit windows of the round as one continuous run (the first
 //    window's gap gives the start), two table steps per loop iteration,
-//    into a private shared-memory slot of nibbles; a warp-shuffle scan
-//    places each run; slots are funnel-shifted into the warp's
-//    output-ordered nibble buffer, whose partial last chunk carries into
-//    the next round.
-//  * Staging and merge.  Each round's bitstream and gaps are staged into
-//    the warp's shared memory with 16-byte cp.async one round ahead (the
-//    copy starts once every lane holds its bytes of the current round in
-//    registers) and its packed sign+mantissa nibbles are loaded into
-//    registers during the decode; exponent and packed nibbles are merged 16
-//    elements at a time with byte-permute/logic ops and written with one
-//    16-byte store.
+//    into a private slot of nibbles (slots are interleaved word by word, so
+//    the lanes' stores fall in distinct banks); a warp-shuffle scan places
+//    each run in the warp's output-ordered nibble buffer.
+//  * Loads straight into registers.  A round's bitstream (16 bytes + 4 bytes
+//    of look-ahead per lane) and gap byte are loaded into registers while the
+//    previous round is placed and merged; its packed sign+mantissa nibbles
+//    are loaded while it decodes.
+//  * Merge in whole-warp steps.  Once the nibble buffer holds 512 elements
+//    past the merge cursor, each lane merges one 16-element chunk per step
+//    (byte-permute/logic ops) and writes it with one 16-byte store; what is
+//    left moves to the front of the buffer for the next round.
 //  * Launch overlap (opt-in, ECF8_DECODE_OVERLAP_PREVIOUS).  With
-//    programmatic dependent launch a decode builds its tables and stages its
+//    programmatic dependent launch a decode builds its tables and loads its
 //    first round while the stream's previous kernel finishes, and writes
 //    outputs only after that kernel has completed (griddepcontrol).
 //
@@ -46,62 +49,69 @@
 
 #include "ecf8.h"
 
+#ifndef ECF8_DECODE_WARPS
+#define ECF8_DECODE_WARPS 27
+#endif
+
 namespace ecf8 {
 namespace {
 
 constexpr int kGroupWindows = ECF8_THREADS_PER_BLOCK;   // windows per group (512)
 constexpr int kWindowBytes = ECF8_BYTES_PER_THREAD;     // bytes per window (8)
 constexpr int kTableThreads = 256;                      // build_table_kernel block size
-constexpr int kWarps = 27;                              // warps per CTA, each decoding its own groups
+constexpr int kWarps = ECF8_DECODE_WARPS;               // warps per CTA, each decoding its own groups
 constexpr int kThreads = kWarps * 32;                   // CTA size
 constexpr int kGroupBytes = kGroupWindows * kWindowBytes;  // 4096
 constexpr int kRoundBytes = 64 * kWindowBytes;          // one round: two windows per lane (512 bytes)
 constexpr int kRounds = kGroupBytes / kRoundBytes;      // rounds per group (8)
-constexpr int kRoundStage = kRoundBytes + 16;           // round bytes + look-ahead, 16-byte units
-constexpr int kRoundGaps = 32;                          // gap bytes per round (4 bits per window)
+constexpr int kRoundReach = kRoundBytes + 4;            // bytes a round reads (look-ahead word of lane 31)
+constexpr int kGapStage = kGroupWindows / 2;            // gap bytes per group
+constexpr int kRoundGaps = kGapStage / kRounds;         // gap bytes per round (32)
 constexpr int kTabBits = 13;                            // multi-symbol table width
 constexpr int kTabSize = 1 << kTabBits;
 constexpr int kMaxSymsPerEntry = 6;                     // 6 nibbles fit in bits 31..8
-constexpr int kSlotWords = 19;                          // 152 nibbles >= 127 + 12 overshoot (odd stride)
+constexpr int kSlotWords = 19;                          // 152 nibbles >= 128 + 12 overshoot
 constexpr int kMaxGroupElems = kGroupWindows * 64;      // one symbol per bit at most
 constexpr int kLutRows = ECF8_MAX_LUTS - 1;             // decode rows (row 0 + prefixes)
-constexpr int kGapStage = kGroupWindows / 2;            // gap bytes per group
-
+constexpr int kStep = 512;                              // elements per merge step (32 lanes x 16)
+// Nibble buffer: up to kStep - 1 pending elements plus one round's codes
+// (at most one per stream bit), 8 per word.
+constexpr int kObufWords = (kStep + kRoundBytes * 8) / 8;
 constexpr int kMaxSmem = 232448;                        // opt-in shared memory per CTA (227 KB)
-constexpr int kTablesBytes = kTabSize * 8 + kLutRows * 256 + 256 + kLutRows * 32 + kTabSize * 2;
-constexpr int kRoundNibbles = 15 + 32 * 128;            // a round's codes plus the carried partial chunk
-// Nibble buffer per warp: one whole round's chunks (16-byte units).
-constexpr int kObufWords = (2 * ((kRoundNibbles + 15) / 16) + 3) / 4 * 4;
+
+// Prepared table (ECF8_TABLE_BYTES): entries, end-offset masks, a copy of the
+// LUTs it was derived from, and a header.
+constexpr int kTabEntryOff = 0;
+constexpr int kTabEndsOff = kTabSize * 8;
+constexpr int kTabLutOff = kTabEndsOff + kTabSize * 2;
+constexpr int kTabHeaderOff = kTabLutOff + ECF8_MAX_LUTS * 256;
+constexpr uint32_t kTabMagic = 0x38464345u;  // "ECF8"
+static_assert(kTabHeaderOff + 16 == ECF8_TABLE_BYTES, "prepared table layout");
 
 // One warp's buffers.
 struct alignas(16) WarpBuf {
-    uint32_t slot[32 * kSlotWords];  // per-lane decoded nibbles (MSB first)
-    uint32_t obuf[kObufWords];       // output-ordered exponent nibbles of one round
-    uint8_t enc[kRoundStage];        // staged bitstream of the next round
-    uint8_t gaps[kRoundGaps];        // staged gaps of the next round
+    uint32_t slot[kSlotWords * 32];  // per-lane decoded nibbles (MSB first); word w of lane l at [32 w + l]
+    uint32_t obuf[kObufWords];       // output-ordered exponent nibbles from the merge cursor on
 };
 static_assert(offsetof(WarpBuf, obuf) % 16 == 0, "obuf must allow 16-byte accesses");
-static_assert(offsetof(WarpBuf, enc) % 16 == 0 && kRoundStage % 16 == 0, "cp.async targets are 16-byte units");
-static_assert(offsetof(WarpBuf, gaps) % 16 == 0, "cp.async alignment");
 static_assert(sizeof(WarpBuf) % 16 == 0, "warp buffers stay 16-byte aligned");
 
 struct alignas(16) Smem {
     uint2 tab[kTabSize];                     // multi-symbol entries (x: entry, y: counter step)
+    uint16_t ends[kTabSize];                 // per entry: bit j set if a symbol other than the last ends at j
     uint8_t lut[kLutRows * 256];             // reference LUT rows 0..n_luts-2, zero padded
     uint8_t lens[256];                       // reference LUT last row: code lengths
     uint32_t chg[kLutRows * 8];              // per row: bit b set if entry b != entry b-1
-    uint16_t ends[kTabSize];                 // per entry: bit j set if a symbol other than the last ends at j
     WarpBuf warp[kWarps];
 };
 static_assert(offsetof(Smem, warp) % 16 == 0 && offsetof(Smem, tab) % 16 == 0 && offsetof(Smem, ends) % 16 == 0,
               "vector copies");
 static_assert(sizeof(Smem) <= kMaxSmem, "fits the opt-in shared memory of one CTA");
-static_assert(offsetof(Smem, warp) == kTablesBytes, "table bytes");
-static_assert(kWarps * 32 * 72 <= 65536, "72 registers per thread");
 
 // Shared-memory layout of build_table_kernel: the decode tables only.
 struct alignas(16) TableSmem {
     uint2 tab[kTabSize];
+    uint16_t ends[kTabSize];
     uint8_t lut[kLutRows * 256];
     uint8_t lens[256];
     uint32_t chg[kLutRows * 8];
@@ -116,15 +126,17 @@ struct DevStream {
     const uint64_t* op;
     const uint8_t* gaps;
     uint8_t* out;
-    const uint32_t* table;  // prepared multi-symbol table (8192 64-bit entries) or null
+    const uint32_t* table;  // prepared table (ECF8_TABLE_BYTES) or null
     long long n_bytes;
     long long n_elements;
     long long n_op;
     long long group_begin;  // first global work index of this stream
     int n_groups;
     int n_luts;
-    int async_ok;           // encoded, packed and gaps 16-byte aligned: cp.async staging
-    int out16;              // outputs 16-byte aligned: 16-byte stores
+    int enc_vec;            // encoded 16-byte aligned: 16-byte loads
+    int packed_vec;         // packed 8-byte aligned: 8-byte loads
+    int out_vec;            // outputs 16-byte aligned: 16-byte stores
+    int pad_;
 };
 
 template <int MAXS>
@@ -134,21 +146,6 @@ struct Batch {
     int pad_;
     DevStream s[MAXS];
 };
-
-// ---------------------------------------------------------------------------
-// Staging: global -> shared copies of 16-byte units, zero-filled past `limit`.
-// ---------------------------------------------------------------------------
-__device__ __forceinline__ void cp_async16(void* dst, const void* src, uint32_t bytes) {
-    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
-
-__device__ __forceinline__ void cp_async16_full(uint32_t dst_s, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst_s), "l"(src) : "memory");
-}
 
 // ---------------------------------------------------------------------------
 // Per-stream set-up.  Entry layout (64 bits): x holds up to six 4-bit
@@ -228,16 +225,15 @@ __device__ __forceinline__ bool real_code(const SM& S, uint32_t v, uint32_t& sym
     return true;
 }
 
-// Copies the stream's LUT rows into shared memory (all threads; ends with a barrier).
+// Copies the stream's LUT rows into shared memory (all threads; no barrier).
 template <class SM>
-__device__ void load_luts(SM& S, const DevStream& d) {
+__device__ void load_luts(SM& S, const uint8_t* luts, int n_luts) {
     const int t = threadIdx.x;
     for (int i = t; i < kLutRows * 256; i += (int)blockDim.x) {
         const int row = i >> 8;
-        S.lut[i] = (row < d.n_luts - 1) ? __ldg(d.luts + i) : (uint8_t)0;
+        S.lut[i] = (row < n_luts - 1) ? __ldg(luts + i) : (uint8_t)0;
     }
-    for (int i = t; i < 256; i += (int)blockDim.x) S.lens[i] = __ldg(d.luts + (d.n_luts - 1) * 256 + i);
-    __syncthreads();
+    for (int i = t; i < 256; i += (int)blockDim.x) S.lens[i] = __ldg(luts + (n_luts - 1) * 256 + i);
 }
 
 // A table entry (64 bits): x = up to six 4-bit symbols, first in bits 31..28,
@@ -249,6 +245,7 @@ __device__ void load_luts(SM& S, const DevStream& d) {
 // long-code path.
 constexpr int kPosShift = 23;                          // counter bit position field: bits 31..23
 constexpr uint32_t kNoCode = 128u << kPosShift;
+constexpr uint32_t kWordField = 0x3ffffu << 5;         // counter word index field: bits 22..5
 __device__ __forceinline__ uint2 make_entry(uint32_t syms, uint32_t bits, uint32_t count) {
     return count ? make_uint2(syms | bits, (bits << kPosShift) | (4 * count)) : make_uint2(0u, kNoCode);
 }
@@ -264,7 +261,8 @@ __device__ __forceinline__ uint2 sanitize_entry(uint2 e) {
     return make_entry(e.x & 0xffffff00u, b, c4 >> 2);
 }
 
-// Derives the multi-symbol table from the LUTs in shared memory (all threads).
+// Derives the multi-symbol table from the LUTs in shared memory (all threads;
+// the LUTs must be visible to every thread).
 template <class SM>
 __device__ void derive_table(SM& S) {
     const int t = threadIdx.x;
@@ -322,51 +320,64 @@ __device__ __forceinline__ uint16_t entry_start_mask(const SM& S, uint2 e) {
     return e.x ? (uint16_t)(entry_ends(S, e) & ((1u << (e.y >> kPosShift)) - 1u)) : (uint16_t)0;
 }
 
-__device__ void build_ends(Smem& S) {
+template <class SM>
+__device__ void build_ends(SM& S) {
     for (int i = threadIdx.x; i < kTabSize; i += (int)blockDim.x) S.ends[i] = entry_start_mask(S, S.tab[i]);
     __syncthreads();
 }
 
-// LUTs plus the table: copied when prepared, derived otherwise (ends with a barrier).
-template <class SM>
-__device__ void setup_stream(SM& S, const DevStream& d) {
-    if (d.table) {  // entries, then the end masks (any mask value is safe)
-        const uint4* src = reinterpret_cast<const uint4*>(d.table);
+// LUTs plus the table (all threads; ends with a barrier).  A prepared table is
+// used only if it was derived from these very LUTs (its stored copy and
+// header match); otherwise, or without one, the CTA derives the table.
+__device__ void setup_stream(Smem& S, const DevStream& d) {
+    load_luts(S, d.luts, d.n_luts);
+    int bad = 1;
+    if (d.table) {
+        const uint8_t* tb = reinterpret_cast<const uint8_t*>(d.table);
+        const uint4* src = reinterpret_cast<const uint4*>(tb + kTabEntryOff);
         uint4* dst = reinterpret_cast<uint4*>(S.tab);
         for (int i = threadIdx.x; i < kTabSize / 2; i += (int)blockDim.x) {
             const uint4 q = __ldg(src + i);
             const uint2 a = sanitize_entry(make_uint2(q.x, q.y)), b = sanitize_entry(make_uint2(q.z, q.w));
             dst[i] = make_uint4(a.x, a.y, b.x, b.y);
         }
+        const uint4* esrc = reinterpret_cast<const uint4*>(tb + kTabEndsOff);
         uint4* ends = reinterpret_cast<uint4*>(S.ends);
-        for (int i = threadIdx.x; i < kTabSize / 8; i += (int)blockDim.x) ends[i] = __ldg(src + kTabSize / 2 + i);
-        load_luts(S, d);
-    } else {
-        load_luts(S, d);
+        for (int i = threadIdx.x; i < kTabSize / 8; i += (int)blockDim.x) ends[i] = __ldg(esrc + i);
+        bad = 0;
+        if (threadIdx.x == 0) {
+            const uint32_t* hdr = reinterpret_cast<const uint32_t*>(tb + kTabHeaderOff);
+            bad = __ldg(hdr) != kTabMagic || __ldg(hdr + 1) != (uint32_t)d.n_luts;
+        }
+        const uint8_t* copy = tb + kTabLutOff;
+        for (int i = threadIdx.x; i < d.n_luts * 256; i += (int)blockDim.x)
+            bad |= __ldg(copy + i) != __ldg(d.luts + i);
+    }
+    if (__syncthreads_or(bad)) {  // also makes the LUTs visible to every thread
         derive_table(S);
         build_ends(S);
     }
 }
 
 // ---------------------------------------------------------------------------
-// Run decode.  A thread's run is its two adjacent windows: stream bits
+// Run decode.  A lane's run is its two adjacent windows: stream bits
 // [gap, 128) of the pair, with the 32 bits after the pair as look-ahead.  The
 // next 160 - p bits sit left-aligned in the shift register h:m:x:y:z.
-// Decoded nibbles go through a 64-bit accumulator (ah:al) into the thread's
-// shared-memory slot.  Returns the number of codes that start in run bits
-// [gap, 128) -- the two windows' counts of decode.cu:65-112 together.
+// Decoded nibbles go through a 64-bit accumulator (ah:al) into the lane's
+// slot.  Returns the number of codes that start in run bits [gap, 128) --
+// the two windows' counts of decode.cu:65-112 together.
 //
 // One counter K carries all of a step's bookkeeping: bits 4..0 are the
-// nibble bits of the open slot word, bits 22..5 that word's shared address / 4
-// (carries out of bit 4 advance it), bits 31..23 the bit position p.  A table
-// entry's y word is the counter step, so one add does it.  The slot store is
-// unconditional (a partly filled word is rewritten until it is full).  The
-// loop takes two table steps per iteration and checks the run's end once,
-// so its last iteration may run up to two steps past bit 128 (at most 12
-// nibbles past the 127 codes before it: the slot has room for 152).  A
-// no-code step moves p by 128 (two of them by 256, within the 9-bit field)
-// and so leaves the loop, whose exit takes the code from the two-level LUT and
-// re-enters; the loop body has no branch of its own.
+// nibble bits of the open slot word, bits 22..5 that word's index in the
+// slot (carries out of bit 4 advance it), bits 31..23 the bit position p.  A
+// table entry's y word is the counter step, so one add does it.  The slot
+// store is unconditional (a partly filled word is rewritten until it is
+// full).  The loop takes two table steps per iteration and checks the run's
+// end once, so its last iteration may run up to two steps past bit 128 (at
+// most 12 nibbles past the 128 codes before it: the slot has room for 152).
+// A no-code step moves p by 128 (two of them by 256, within the 9-bit field)
+// and so leaves the loop, whose exit takes the code from the two-level LUT
+// and re-enters; the loop body has no branch of its own.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void lds64(uint32_t a, uint32_t& lo, uint32_t& hi) {
     asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(lo), "=r"(hi) : "r"(a));
@@ -374,9 +385,12 @@ __device__ __forceinline__ void lds64(uint32_t a, uint32_t& lo, uint32_t& hi) {
 __device__ __forceinline__ void sts32(uint32_t a, uint32_t v) {
     asm volatile("st.shared.u32 [%0], %1;" ::"r"(a), "r"(v) : "memory");
 }
+// Shared address of the slot word whose index is K's word field, for the
+// lane whose word 0 is at lane_s (word w at lane_s + 128 w).
+__device__ __forceinline__ uint32_t slot_addr(uint32_t lane_s, uint32_t K) { return lane_s + ((K & kWordField) << 2); }
 
 // w3, w4: the run's stream bytes 12..19 (bits 96..159), for the end fix-up.
-__device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, uint32_t w0, uint32_t w1,
+__device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t lane_s, uint32_t w0, uint32_t w1,
                                                uint32_t w2, uint32_t w3, uint32_t w4, uint32_t gap) {
     const uint32_t tab_s = (uint32_t)__cvta_generic_to_shared(S.tab);
     uint32_t h = __funnelshift_l(w1, w0, gap);
@@ -384,7 +398,7 @@ __device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, u
     uint32_t x = __funnelshift_l(w3, w2, gap);
     uint32_t y = __funnelshift_l(w4, w3, gap);
     uint32_t z = w4 << gap;
-    uint32_t K = (gap << kPosShift) | ((slot_s >> 2) << 5);
+    uint32_t K = gap << kPosShift;
     uint32_t ah = 0, al = 0, elo1, ehi1, elo2, ehi2;
 #pragma unroll 1
     for (;;) {
@@ -395,12 +409,12 @@ __device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, u
             lds64(tab_s + ((h >> (32 - kTabBits)) << 3), elo1, ehi1);
             const uint32_t h1 = __funnelshift_l(m, h, elo1);
             lds64(tab_s + ((h1 >> (32 - kTabBits)) << 3), elo2, ehi2);
-            const uint32_t sa1 = (K >> 3) & 0xffffcu;
+            const uint32_t sa1 = slot_addr(lane_s, K);
             ah = __funnelshift_l(al, ah, ehi1);  // append the entry's symbols; shift = ehi & 31 = 4 x count
             al = __funnelshift_l(elo1, al, ehi1);
             K += ehi1;
             sts32(sa1, __funnelshift_r(al, ah, K));
-            const uint32_t sa2 = (K >> 3) & 0xffffcu;
+            const uint32_t sa2 = slot_addr(lane_s, K);
             ah = __funnelshift_l(al, ah, ehi2);
             al = __funnelshift_l(elo2, al, ehi2);
             K += ehi2;
@@ -430,7 +444,7 @@ __device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, u
         elo1 = ((sym & 15u) << 28) | len;
         ehi1 = (len << kPosShift) | 4u;
         elo2 = ehi2 = 0u;
-        const uint32_t sa = (K >> 3) & 0xffffcu;
+        const uint32_t sa = slot_addr(lane_s, K);
         ah = __funnelshift_l(al, ah, ehi1);
         al = __funnelshift_l(elo1, al, ehi1);
         K += ehi1;
@@ -443,8 +457,8 @@ __device__ __forceinline__ uint32_t decode_run(const Smem& S, uint32_t slot_s, u
         if (K >= (128u << kPosShift)) break;
     }
     const uint32_t m4 = K & 31u;
-    const uint32_t words = ((K >> 5) & 0x3ffffu) - (slot_s >> 2);
-    if (m4) sts32(slot_s + 4 * words, al << (32 - m4));
+    const uint32_t words = (K & kWordField) >> 5;
+    if (m4) sts32(slot_addr(lane_s, K), al << (32 - m4));
     uint32_t n = words * 8 + (m4 >> 2);
     // The last iteration may have taken codes that start at or after the
     // run's end; they belong to the next run.  Its second step started at p1,
@@ -493,6 +507,13 @@ __device__ __forceinline__ void merge8(uint32_t ew, uint32_t pw, uint32_t& lo, u
     hi = __byte_perm(ev, od, 0x7362);
 }
 
+__device__ __forceinline__ uint4 merge16(uint2 ew, uint2 p) {
+    uint4 o;
+    merge8(ew.x, p.x, o.x, o.y);
+    merge8(ew.y, p.y, o.z, o.w);
+    return o;
+}
+
 // Output range of group g: [output_positions[g], output_positions[g+1])
 // (decode.cu:116,144-145,208), an entry the array lacks counting as n_elements.
 struct GroupRange {
@@ -518,19 +539,32 @@ __device__ __forceinline__ int find_stream(const DevStream* s, int from, long lo
 // at or past n_elements / 2 read as 0.
 __device__ __forceinline__ uint2 packed8(const DevStream& d, unsigned long long off) {
     const unsigned long long limit = (unsigned long long)d.n_elements >> 1;
-    if (d.async_ok && off + 8 <= limit) return __ldg(reinterpret_cast<const uint2*>(d.packed + off));
+    if (d.packed_vec && off + 8 <= limit) return __ldg(reinterpret_cast<const uint2*>(d.packed + off));
     uint32_t b[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) b[k] = off + k < limit ? __ldg(d.packed + off + k) : 0u;
     return make_uint2(b[0] | b[1] << 8 | b[2] << 16 | b[3] << 24, b[4] | b[5] << 8 | b[6] << 16 | b[7] << 24);
 }
 
+// Merges output chunk c (16 elements from base + 16c) and stores the
+// elements inside [lo, hi) (relative to base) byte by byte.
+__device__ __forceinline__ void store_bytes(const DevStream& d, unsigned long long base, uint32_t c, uint2 ew,
+                                            uint2 p, uint32_t lo, uint32_t hi) {
+    const uint4 o = merge16(ew, p);
+    const uint32_t ow[4] = {o.x, o.y, o.z, o.w};
+    uint8_t* dst = d.out + base;
+    const uint32_t e0 = 16u * c;
+#pragma unroll
+    for (int k = 0; k < 16; ++k)
+        if (e0 + k >= lo && e0 + k < hi) dst[e0 + k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
+}
+
 // Copies run nibbles [dpos, dpos + n) (output positions relative to the
-// nibble buffer's word 0) from the run's slot into the buffer.  The run's
-// first and last words are shared with the neighbouring runs (atomicOr into
-// the zeroed buffer); the words in between are its own.  Reading slot[nw]
-// when nw is the slot size stays in shared memory (the next slot or the
-// buffer) and is masked off by `tail`.
+// nibble buffer's word 0) from the lane's slot (word q at slot[32 q]) into
+// the buffer.  The run's first and last words are shared with the
+// neighbouring runs (atomicOr into the zeroed buffer); the words in between
+// are its own.  Reading slot word nw when it is past the run's last written
+// word stays inside the slot and is masked off by `tail`.
 __device__ __forceinline__ void place_run(uint32_t* obuf, const uint32_t* slot, uint32_t dpos, uint32_t n) {
     const uint32_t e = dpos + n;
     const uint32_t nw = ((e - 1) >> 3) - (dpos >> 3);  // words after the first
@@ -541,250 +575,248 @@ __device__ __forceinline__ void place_run(uint32_t* obuf, const uint32_t* slot, 
     atomicOr(obuf + o0, (prev >> sh) & (nw ? 0xffffffffu : tail));
     uint32_t q = 1;
     for (; q + 1 < nw; q += 2) {
-        const uint32_t c0 = slot[q], c1 = slot[q + 1];
+        const uint32_t c0 = slot[32 * q], c1 = slot[32 * (q + 1)];
         obuf[o0 + q] = __funnelshift_r(c0, prev, sh);
         obuf[o0 + q + 1] = __funnelshift_r(c1, c0, sh);
         prev = c1;
     }
     if (q < nw) {
-        const uint32_t c0 = slot[q];
+        const uint32_t c0 = slot[32 * q];
         obuf[o0 + q] = __funnelshift_r(c0, prev, sh);
         prev = c0;
     }
-    if (nw) atomicOr(obuf + o0 + nw, __funnelshift_r(slot[nw], prev, sh) & tail);
+    if (nw) atomicOr(obuf + o0 + nw, __funnelshift_r(slot[32 * nw], prev, sh) & tail);
 }
 
-// Stages round r of group g (its 512 stream bytes plus 16 bytes of
-// look-ahead, and its 32 gap bytes) into buffer b of the warp, zero-filled
-// past the end of the stream.  cp.async when the stream's buffers are 16-byte
-// aligned, plain loads otherwise.  The lanes read each other's bytes only
-// after the warp's next __syncwarp.
-__device__ __forceinline__ void stage_round(WarpBuf& W, const DevStream& d, int g, int r, int lane) {
-    const long long lo = (long long)g * kGroupBytes + (long long)r * kRoundBytes;
-    const uint32_t eb = (uint32_t)__cvta_generic_to_shared(W.enc);
-    if (d.async_ok && lo + kRoundStage <= d.n_bytes) {
-        cp_async16_full(eb + 16 * lane, d.encoded + lo + 16 * lane);
-        if (lane == 0) cp_async16_full(eb + kRoundBytes, d.encoded + lo + kRoundBytes);
+// One round's input for one lane: its 16 stream bytes plus 4 bytes of
+// look-ahead (as loaded: little-endian words of the big-endian stream) and
+// its gap byte (the gap of its first window in the high nibble).
+struct RoundIn {
+    uint32_t w0, w1, w2, w3, w4, gap;
+};
+
+// Loads the round at stream byte `lo` with gap bytes `gp`; stream bytes at or
+// past n_bytes read as 0.
+__device__ __forceinline__ void load_round(RoundIn& in, const DevStream& d, long long lo, const uint8_t* gp,
+                                           int lane) {
+    in.gap = __ldg(gp + lane);  // gaps exist for every group (n_gap_bytes >= groups x 256)
+    const long long off = lo + 16 * lane;
+    if (d.enc_vec && lo + kRoundReach <= d.n_bytes) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(d.encoded + off));
+        in.w0 = v.x;
+        in.w1 = v.y;
+        in.w2 = v.z;
+        in.w3 = v.w;
+        in.w4 = __ldg(reinterpret_cast<const uint32_t*>(d.encoded + off + 16));
     } else {
-        const long long vl = d.n_bytes - lo;
-        for (int i = 16 * lane; i < kRoundStage; i += 32 * 16) {
-            const int v = (int)min(max(vl - i, 0ll), 16ll);  // bytes of this unit inside the stream
-            if (d.async_ok) {
-                cp_async16(W.enc + i, v ? d.encoded + lo + i : d.encoded, (uint32_t)v);
-            } else {
+        uint32_t w[5];
 #pragma unroll
-                for (int k = 0; k < 16; ++k) W.enc[i + k] = k < v ? __ldg(d.encoded + lo + i + k) : (uint8_t)0;
+        for (int k = 0; k < 5; ++k) {
+            uint32_t v = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const long long o = off + 4 * k + j;
+                v |= (o < d.n_bytes ? (uint32_t)__ldg(d.encoded + o) : 0u) << (8 * j);
             }
+            w[k] = v;
         }
-    }
-    const long long glo = (long long)g * kGapStage + (long long)r * kRoundGaps;  // gaps exist for every group
-    if (d.async_ok) {
-        if (lane < kRoundGaps / 16)
-            cp_async16_full((uint32_t)__cvta_generic_to_shared(W.gaps) + 16 * lane, d.gaps + glo + 16 * lane);
-    } else {
-        W.gaps[lane] = __ldg(d.gaps + glo + lane);
+        in.w0 = w[0];
+        in.w1 = w[1];
+        in.w2 = w[2];
+        in.w3 = w[3];
+        in.w4 = w[4];
     }
 }
 
-// Packed words of chunks C + lane + 32k (k < 4) of the group at `base`,
-// those entirely below the group's end `re`; loaded while the round decodes.
+// Packed words of chunks C + lane + 32k (k < 4) of the output at `base`,
+// those below `climit` (chunks whose 16 elements lie below n_elements); the
+// merge steps of the next round use them.
 __device__ __forceinline__ void prefetch_packed(uint2 (&pw)[4], const DevStream& d, unsigned long long base,
-                                                uint32_t C, uint32_t re, int lane) {
-    const uint2* src = reinterpret_cast<const uint2*>(d.packed + (base >> 1));
+                                                uint32_t C, uint32_t climit, int lane) {
+    if (d.packed_vec) {
+        const uint2* src = reinterpret_cast<const uint2*>(d.packed + (base >> 1));
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const uint32_t c = C + lane + 32 * k;
-        pw[k] = c < (re >> 4) ? __ldg(src + c) : make_uint2(0u, 0u);
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t c = C + lane + 32 * k;
+            pw[k] = c < climit ? __ldg(src + c) : make_uint2(0u, 0u);
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t c = C + lane + 32 * k;
+            pw[k] = c < climit ? packed8(d, (base >> 1) + 8ull * c) : make_uint2(0u, 0u);
+        }
     }
 }
 
-// Merges output chunk c (16 elements from base + 16c) and stores the
-// elements inside the group's range [rs, re) byte by byte.
-__device__ __forceinline__ void store_bytes(const DevStream& d, unsigned long long base, uint32_t c, uint2 ew,
-                                            uint2 p, uint32_t rs, uint32_t re) {
-    uint32_t ow[4];
-    merge8(ew.x, p.x, ow[0], ow[1]);
-    merge8(ew.y, p.y, ow[2], ow[3]);
-    uint8_t* dst = d.out + base;
-    const uint32_t e0 = 16u * c;
-#pragma unroll
-    for (int k = 0; k < 16; ++k)
-        if (e0 + k >= rs && e0 + k < re) dst[e0 + k] = (uint8_t)(ow[k >> 2] >> (8 * (k & 3)));
-}
-
-// Merges and stores the round's complete chunks [C, Cn); the nibble buffer
-// holds chunk C at word 0 and every word read is zeroed again.  Chunk
-// C + lane + 32k takes the prefetched packed word pw[k]; chunks from C + 128
-// on (highly compressed rounds) load theirs here.  Lane 0 merges chunk C and
-// then moves the round's partial last chunk Cn (if any) to word 0 for the
-// next round, so no other lane touches words 0..1.  The group's partial first
-// chunk (c = 0 when rs > 0) and all chunks of unaligned streams are stored
-// byte by byte.
-__device__ __forceinline__ void merge_round(WarpBuf& W, const DevStream& d, unsigned long long base, uint32_t rs,
-                                            uint32_t re, uint32_t C, uint32_t Cn, uint32_t Pn, int lane, bool fast,
+// Merges `steps` whole steps: lane l merges chunks C + l + 32k (k < steps),
+// all complete and below n_elements, and zeroes the buffer words it read.
+// Chunk 0 is partial when head > 0 (its first `head` elements belong to the
+// range before this one) and is written byte by byte.
+__device__ __forceinline__ void merge_steps(uint32_t* obuf, const DevStream& d, unsigned long long base,
+                                            uint32_t C, uint32_t steps, uint32_t head, int lane,
                                             const uint2 (&pw)[4]) {
-    uint2* ew2 = reinterpret_cast<uint2*>(W.obuf);
-    uint4* ob = reinterpret_cast<uint4*>(d.out + base);
+    uint2* ew2 = reinterpret_cast<uint2*>(obuf) + lane;
+    uint4* ob = reinterpret_cast<uint4*>(d.out + base) + C + lane;
+    const uint32_t c0 = C + lane;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        const uint32_t c = C + lane + 32 * k;
-        if (c < Cn) {
-            const uint2 ew = ew2[c - C];
-            ew2[c - C] = make_uint2(0u, 0u);
-            if (fast && (c || !rs)) {
-                uint4 o;
-                merge8(ew.x, pw[k].x, o.x, o.y);
-                merge8(ew.y, pw[k].y, o.z, o.w);
-                ob[c] = o;
-            } else {
-                store_bytes(d, base, c, ew, fast ? pw[k] : packed8(d, (base >> 1) + 8ull * c), rs, re);
-            }
+        if ((uint32_t)k < steps) {
+            const uint2 ew = ew2[32 * k];
+            ew2[32 * k] = make_uint2(0u, 0u);
+            const uint32_t c = c0 + 32 * k;
+            if (d.out_vec && (c | (head == 0)))
+                ob[32 * k] = merge16(ew, pw[k]);
+            else
+                store_bytes(d, base, c, ew, pw[k], c ? 0u : head, 16u * c + 16u);
         }
     }
-    for (uint32_t c = C + 128 + lane; c < Cn; c += 32) {
-        const uint2 ew = ew2[c - C];
-        ew2[c - C] = make_uint2(0u, 0u);
+    for (uint32_t k = 4; k < steps; ++k) {  // highly compressed rounds only
+        const uint2 ew = ew2[32 * k];
+        ew2[32 * k] = make_uint2(0u, 0u);
+        const uint32_t c = c0 + 32 * k;
         const uint2 p = packed8(d, (base >> 1) + 8ull * c);
-        if (fast) {
-            uint4 o;
-            merge8(ew.x, p.x, o.x, o.y);
-            merge8(ew.y, p.y, o.z, o.w);
-            ob[c] = o;
-        } else {
-            store_bytes(d, base, c, ew, p, rs, re);
-        }
-    }
-    if (lane == 0 && Cn > C && (Pn & 15u)) {
-        ew2[0] = ew2[Cn - C];
-        ew2[Cn - C] = make_uint2(0u, 0u);
+        if (d.out_vec)
+            ob[32 * k] = merge16(ew, p);
+        else
+            store_bytes(d, base, c, ew, p, 0u, 16u * c + 16u);
     }
 }
 
-// After a group's last round: chunks [Cn, ceil(re / 16)) -- the partial last
-// chunk, whose nibbles sit at word 0, and any chunk the stream's codes did not
-// reach (exponent 0) -- stored byte by byte; word 0 is zeroed again.
-__device__ __forceinline__ void flush_group(WarpBuf& W, const DevStream& d, unsigned long long base, uint32_t rs,
-                                            uint32_t re, uint32_t Cn, int lane) {
-    uint2* ew2 = reinterpret_cast<uint2*>(W.obuf);
-    const uint32_t n_chunks = (re + 15) >> 4;
-    for (uint32_t c = Cn + lane; c < n_chunks; c += 32) {
+// Writes chunks [C, ceil(lim / 16)) of the output at `base`: the pending
+// chunks in the buffer, the last one partial, and any chunk past them that
+// the codes did not reach (exponent 0); elements below `head` in chunk 0 and
+// from `lim` on are left alone.  Zeroes the buffer words it reads.
+__device__ void flush_pending(uint32_t* obuf, const DevStream& d, unsigned long long base, uint32_t C,
+                              uint32_t lim, uint32_t head, int lane) {
+    uint2* ew2 = reinterpret_cast<uint2*>(obuf);
+    const uint32_t end = (lim + 15) >> 4;
+    for (uint32_t c = C + lane; c < end; c += 32) {
+        const uint32_t j = c - C;
         uint2 ew = make_uint2(0u, 0u);
-        if (c == Cn) {
-            ew = ew2[0];
-            ew2[0] = make_uint2(0u, 0u);
+        if (j < (uint32_t)(kObufWords / 2)) {
+            ew = ew2[j];
+            ew2[j] = make_uint2(0u, 0u);
         }
-        store_bytes(d, base, c, ew, packed8(d, (base >> 1) + 8ull * c), rs, re);
+        const uint32_t lo = c ? 0u : head;
+        const uint2 p = packed8(d, (base >> 1) + 8ull * c);
+        if (d.out_vec && lo == 0 && 16u * c + 16u <= lim)
+            reinterpret_cast<uint4*>(d.out + base)[c] = merge16(ew, p);
+        else
+            store_bytes(d, base, c, ew, p, lo, lim);
     }
 }
 
-// Stream bytes from round r of group g on.
-__device__ __forceinline__ long long rem_of(long long n_bytes, int g, int r) {
-    return n_bytes - (long long)g * kGroupBytes - (long long)r * kRoundBytes;
+// Full 16-element chunks of the output at `base` below n_elements.
+__device__ __forceinline__ uint32_t chunk_limit(const DevStream& d, unsigned long long base) {
+    const unsigned long long n = ((unsigned long long)d.n_elements - base) >> 4;
+    return n > 0x7fffffffull ? 0x7fffffffu : (uint32_t)n;
 }
 
-// One warp decodes groups g0, g0 + kWarps, ... below g_end of stream d, each
-// in eight rounds of 64 windows: lane i decodes windows 2i and 2i + 1 of the
-// round as one run into its slot, a warp-shuffle scan places the runs, and
-// the round's complete 16-element chunks are merged and stored.  The output
-// position P (relative to the group's 16-aligned base) carries from round to
-// round, and with it the partial chunk that holds P.  Only __syncwarp
-// orders the lanes: one after the placement (nibble buffer complete), one
-// after the merge (buffer zero again but for the carried chunk, next round's
-// staged bytes visible).  The next round is staged and its packed words are
-// loaded while the current round decodes.
-__device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int g0, int g_end, int lane) {
-    uint32_t* slot = W.slot + lane * kSlotWords;
-    const uint32_t slot_s = (uint32_t)__cvta_generic_to_shared(slot);
-    const long long n_bytes = d.n_bytes;
-    const bool fast = d.out16 && d.async_ok;
-    // The first round's bytes and the first group's range are fetched while
-    // the CTA sets up the stream's tables (all warps take part; ends with a barrier).
-    GroupRange rg{0, 0};
-    if (g0 < g_end) {
-        for (int i = lane; i < kObufWords / 4; i += 32) reinterpret_cast<uint4*>(W.obuf)[i] = make_uint4(0, 0, 0, 0);
-        stage_round(W, d, g0, 0, lane);
-        rg = group_range(d, g0);
+// One warp decodes groups [ga, gb) of stream d, in rounds of 64 windows:
+// lane i decodes windows 2i and 2i + 1 of the round as one run into its
+// slot, a warp-shuffle scan places the runs after the output position P, and
+// whole merge steps are merged and stored.  P, the merge cursor C (a chunk
+// index) and the buffer carry from round to round and from group to group;
+// all are relative to `base`, the output position (16-aligned) of the
+// range's first chunk.  A group that does not start where the previous one
+// ended (a stream the reference compressor did not write) flushes the buffer
+// and starts a new range.  Only __syncwarp orders the lanes.
+__device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int ga, int gb, int lane) {
+    uint32_t* obuf = W.obuf;
+    const uint32_t lane_s = (uint32_t)__cvta_generic_to_shared(W.slot + lane);
+    const bool have = ga < gb;
+    RoundIn in{};
+    uint2 pw[4];
+    unsigned long long base = 0;
+    uint32_t P = 0, head = 0, re = 0, climit = 0, C = 0;
+    // The first round's input and the first packed words are loaded while the
+    // CTA sets up the stream's tables (all warps take part; ends with a barrier).
+    if (have) {
+        const GroupRange rg = group_range(d, ga);
+        load_round(in, d, (long long)ga * kGroupBytes, d.gaps + (long long)ga * kGapStage, lane);
+        base = rg.start & ~15ull;
+        P = head = (uint32_t)(rg.start - base);
+        re = (uint32_t)(rg.end - base);
+        climit = chunk_limit(d, base);
+        prefetch_packed(pw, d, base, 0, climit, lane);
     }
-    cp_async_commit();
     setup_stream(S, d);
     // Under programmatic dependent launch (ECF8_DECODE_OVERLAP_PREVIOUS) the
     // set-up above may run while the stream's previous kernel finishes; the
     // outputs are written only after it has completed.  Without that launch
     // attribute this returns at once.
     asm volatile("griddepcontrol.wait;" ::: "memory");
-    if (g0 >= g_end) return;
-    cp_async_wait<0>();
-    __syncwarp();
+    if (!have) return;
 
-    int g = g0, r = 0;
-    unsigned long long base = rg.start & ~15ull;
-    uint32_t rs = (uint32_t)(rg.start - base), re = (uint32_t)(rg.end - base), P = rs;
-    GroupRange rn = g + kWarps < g_end ? group_range(d, g + kWarps) : GroupRange{0, 0};
-    uint2 pw[4];
-    if (fast) prefetch_packed(pw, d, base, 0, re, lane);
+    int g = ga, r = 0;
+    long long lo = (long long)ga * kGroupBytes;
+    GroupRange rn = g + 1 < gb ? group_range(d, g + 1) : GroupRange{0, 0};
 #pragma unroll 1
     for (;;) {
-        const bool last_round = r == kRounds - 1;
-        // This lane's window pair of the staged round; then the buffer takes the next round.
-        const bool active = rem_of(n_bytes, g, r) > 16 * lane;
-        uint4 raw = make_uint4(0u, 0u, 0u, 0u);
-        uint32_t r4 = 0u, gap = 0u;
-        if (active) {
-            raw = *reinterpret_cast<const uint4*>(W.enc + 16 * lane);
-            r4 = *reinterpret_cast<const uint32_t*>(W.enc + 16 * lane + 16);
-            gap = W.gaps[lane] >> 4;
-        }
-        __syncwarp();
-        if (!last_round)
-            stage_round(W, d, g, r + 1, lane);
-        else if (g + kWarps < g_end)
-            stage_round(W, d, g + kWarps, 0, lane);
-        cp_async_commit();
-
         // --- decode this lane's window pair ---
         uint32_t count = 0;
-        if (active)
-            count = decode_run(S, slot_s, __byte_perm(raw.x, 0, 0x0123), __byte_perm(raw.y, 0, 0x0123),
-                               __byte_perm(raw.z, 0, 0x0123), __byte_perm(raw.w, 0, 0x0123),
-                               __byte_perm(r4, 0, 0x0123), gap);
-        // A pair wholly past n_bytes only follows the last real code: it places nothing.
+        if (d.n_bytes - lo > 16 * lane)  // a pair wholly past n_bytes only follows the last real code
+            count = decode_run(S, lane_s, __byte_perm(in.w0, 0, 0x0123), __byte_perm(in.w1, 0, 0x0123),
+                               __byte_perm(in.w2, 0, 0x0123), __byte_perm(in.w3, 0, 0x0123),
+                               __byte_perm(in.w4, 0, 0x0123), in.gap >> 4);
+        // --- the next round's input: the group's next round, else the next group's first ---
+        const bool next_in_group = r + 1 < kRounds && lo + kRoundBytes < d.n_bytes;
+        const int gn = next_in_group ? g : g + 1;
+        const int rnext = next_in_group ? r + 1 : 0;
+        const bool more = gn < gb;
+        const long long lon = (long long)gn * kGroupBytes + (long long)rnext * kRoundBytes;
+        if (more) load_round(in, d, lon, d.gaps + (long long)gn * kGapStage + rnext * kRoundGaps, lane);
 
         // --- exclusive scan of run counts (decode.cu:114-148) ---
         uint32_t v = count;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t y = __shfl_up_sync(0xffffffffu, v, o);
-            if (lane >= o) v += y;
+            const uint32_t t = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += t;
         }
         const uint32_t total = __shfl_sync(0xffffffffu, v, 31);
-        const uint32_t C = P >> 4;
         const uint32_t dpos = P + v - count;
         const uint32_t n_place = (count && dpos < re) ? min(count, re - dpos) : 0u;
         const uint32_t Pn = min(P + total, re);
-        const uint32_t Cn = Pn >> 4;
-        if (n_place) place_run(W.obuf, slot, dpos - 16u * C, n_place);
+        if (n_place) place_run(obuf, W.slot + lane, dpos - 16u * C, n_place);
         __syncwarp();
-        merge_round(W, d, base, rs, re, C, Cn, Pn, lane, fast, pw);
-        cp_async_wait<0>();  // this lane's copies of the next round
+        // --- whole merge steps, then the rest moves to the buffer's front ---
+        const uint32_t steps = (Pn - 16u * C) / kStep;
+        if (steps) {
+            merge_steps(obuf, d, base, C, steps, head, lane, pw);
+            uint2* ew2 = reinterpret_cast<uint2*>(obuf);
+            const uint2 t = ew2[32 * steps + lane];
+            ew2[32 * steps + lane] = make_uint2(0u, 0u);
+            ew2[lane] = t;
+            C += 32 * steps;
+        }
         __syncwarp();
         P = Pn;
-        if (!last_round) {
-            ++r;
-            if (fast) prefetch_packed(pw, d, base, Cn, re, lane);
-            continue;
+        if (!more) break;
+        if (gn != g) {
+            // The next group continues this range if it starts where this
+            // group ended (always, for a stream the reference compressor
+            // wrote); otherwise the range ends here and a new one begins.
+            const GroupRange rg = rn;
+            g = gn;
+            rn = g + 1 < gb ? group_range(d, g + 1) : GroupRange{0, 0};
+            if (rg.start < base || rg.start - base != P || P > (1u << 30)) {
+                flush_pending(obuf, d, base, C, re, head, lane);
+                __syncwarp();
+                base = rg.start & ~15ull;
+                P = head = (uint32_t)(rg.start - base);
+                C = 0;
+                climit = chunk_limit(d, base);
+            }
+            re = (uint32_t)(rg.end - base);
         }
-        flush_group(W, d, base, rs, re, Cn, lane);
-        __syncwarp();
-        g += kWarps;
-        if (g >= g_end) break;
-        r = 0;
-        base = rn.start & ~15ull;
-        rs = (uint32_t)(rn.start - base);
-        re = (uint32_t)(rn.end - base);
-        P = rs;
-        if (g + kWarps < g_end) rn = group_range(d, g + kWarps);
-        if (fast) prefetch_packed(pw, d, base, 0, re, lane);
+        r = rnext;
+        lo = lon;
+        prefetch_packed(pw, d, base, C, climit, lane);
     }
+    flush_pending(obuf, d, base, C, re, head, lane);
+    __syncwarp();
 }
 
 template <int MAXS>
@@ -800,15 +832,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     const long long lo = (long long)blockIdx.x * total / gridDim.x;
     const long long hi = (long long)(blockIdx.x + 1) * total / gridDim.x;
     if (lo >= hi) return;
+    // Every warp's nibble buffer starts zeroed and each segment leaves it so.
+    WarpBuf& W = S.warp[warp];
+    for (int i = lane; i < kObufWords / 4; i += 32) reinterpret_cast<uint4*>(W.obuf)[i] = make_uint4(0, 0, 0, 0);
+    __syncwarp();
 
     // The CTA's range [lo, hi) in per-stream segments: the tables of one
-    // stream at a time, each warp taking every kWarps-th group of the segment.
+    // stream at a time, each warp taking a contiguous share of the segment.
     int si = find_stream(B.s, 0, lo);
     long long w = lo;
     for (;;) {
         const DevStream& d = B.s[si];
         const long long seg_end = min(hi, d.group_begin + d.n_groups);
-        decode_warp(S, S.warp[warp], d, (int)(w - d.group_begin) + warp, (int)(seg_end - d.group_begin), lane);
+        const long long s0 = w - d.group_begin, len = seg_end - w;
+        const int ga = (int)(s0 + len * warp / kWarps), gb = (int)(s0 + len * (warp + 1) / kWarps);
+        decode_warp(S, W, d, ga, gb, lane);
         if (seg_end >= hi) break;
         w = seg_end;
         si = find_stream(B.s, si, w);
@@ -816,21 +854,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_consta
     }
 }
 
-// One CTA derives a stream's multi-symbol table and writes it to `table`.
+// One CTA derives a stream's multi-symbol table and writes it, with a copy of
+// the LUTs and the header, to `table`.
 __global__ void __launch_bounds__(kTableThreads, 1) build_table_kernel(const uint8_t* luts, int n_luts,
                                                                        uint32_t* table) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     TableSmem& S = *reinterpret_cast<TableSmem*>(smem_raw);
-    DevStream d{};
-    d.luts = luts;
-    d.n_luts = n_luts;
-    load_luts(S, d);
+    load_luts(S, luts, n_luts);
+    __syncthreads();
     derive_table(S);
-    uint2* out = reinterpret_cast<uint2*>(table);
-    uint16_t* ends = reinterpret_cast<uint16_t*>(out + kTabSize);
+    uint8_t* tb = reinterpret_cast<uint8_t*>(table);
+    uint2* out = reinterpret_cast<uint2*>(tb + kTabEntryOff);
+    uint16_t* ends = reinterpret_cast<uint16_t*>(tb + kTabEndsOff);
     for (int i = threadIdx.x; i < kTabSize; i += (int)blockDim.x) {
         out[i] = S.tab[i];
         ends[i] = entry_start_mask(S, S.tab[i]);
+    }
+    uint8_t* copy = tb + kTabLutOff;
+    for (int i = threadIdx.x; i < ECF8_MAX_LUTS * 256; i += (int)blockDim.x)
+        copy[i] = i < n_luts * 256 ? __ldg(luts + i) : (uint8_t)0;
+    if (threadIdx.x == 0) {
+        uint32_t* hdr = reinterpret_cast<uint32_t*>(tb + kTabHeaderOff);
+        hdr[0] = kTabMagic;
+        hdr[1] = (uint32_t)n_luts;
+        hdr[2] = ECF8_ABI_VERSION;
+        hdr[3] = 0;
     }
 }
 
@@ -846,23 +894,26 @@ struct DeviceInfo {
 
 constexpr int kMaxDevices = 64;
 DeviceInfo g_devices[kMaxDevices];
-std::once_flag g_device_once[kMaxDevices];
-int g_device_status[kMaxDevices];
+bool g_device_ready[kMaxDevices];
+std::mutex g_device_mutex;
 
 int cuda_fail(cudaError_t e) {
     g_last_cuda_error = (int)e;
     return ECF8_ERR_CUDA;
 }
 
+// Launch attributes of the current device, set up on its first use.  A failed
+// set-up is not remembered: the next call tries again.
 int device_info(DeviceInfo* out) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e);
     if (dev < 0 || dev >= kMaxDevices) return ECF8_ERR_UNSUPPORTED;
-    std::call_once(g_device_once[dev], [dev]() {
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    if (!g_device_ready[dev]) {
         DeviceInfo info;
-        cudaError_t err = cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, dev);
         const int smem = (int)sizeof(Smem);
+        cudaError_t err = cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, dev);
         if (err == cudaSuccess)
             err = cudaFuncSetAttribute(decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (err == cudaSuccess)
@@ -874,12 +925,12 @@ int device_info(DeviceInfo* out) {
         if (err == cudaSuccess)
             err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&info.blocks_per_sm, decode_kernel<1>,
                                                                 kThreads, smem);
-        g_device_status[dev] = (int)err;
+        if (err != cudaSuccess) return cuda_fail(err);
+        if (info.blocks_per_sm < 1) info.blocks_per_sm = 1;
         g_devices[dev] = info;
-    });
-    if (g_device_status[dev] != cudaSuccess) return cuda_fail((cudaError_t)g_device_status[dev]);
+        g_device_ready[dev] = true;
+    }
     *out = g_devices[dev];
-    if (out->blocks_per_sm < 1) out->blocks_per_sm = 1;
     return ECF8_OK;
 }
 
@@ -913,8 +964,10 @@ int make_stream(const ecf8_stream& s, DevStream* d) {
     d->n_luts = s.n_luts;
     // A stream with no elements has nothing to place.
     d->n_groups = s.n_elements > 0 ? (int)groups : 0;
-    d->async_ok = aligned(s.encoded, 16) && aligned(s.packed_other_4bits, 16) && aligned(s.gaps, 16);
-    d->out16 = aligned(s.outputs, 16);
+    d->enc_vec = aligned(s.encoded, 16);
+    d->packed_vec = aligned(s.packed_other_4bits, 8);
+    d->out_vec = aligned(s.outputs, 16);
+    d->pad_ = 0;
     d->group_begin = 0;
     return ECF8_OK;
 }
@@ -989,7 +1042,6 @@ int decode_batch(const ecf8_stream* streams, int n_streams, int threads_per_bloc
     }
     return ECF8_OK;
 }
-
 
 }  // namespace
 }  // namespace ecf8

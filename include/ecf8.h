@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ECF8_ABI_VERSION 6
+#define ECF8_ABI_VERSION 7
 
 /* Status codes. */
 #define ECF8_OK 0
@@ -46,7 +46,7 @@ extern "C" {
 #define ECF8_THREADS_PER_BLOCK 512 /* windows per group (compress.py:7) */
 #define ECF8_MAX_LUTS 18           /* row 0 + 16 prefix rows + length row */
 #define ECF8_MAX_BATCH 128         /* streams per ecf8_decode_batch launch */
-#define ECF8_TABLE_BYTES 81920     /* prepared decode table (ecf8_build_table) */
+#define ECF8_TABLE_BYTES 86544     /* prepared decode table (ecf8_build_table) */
 
 /* One stream of a batched decode; field meaning as in ecf8_decode(). */
 typedef struct ecf8_stream {
@@ -92,15 +92,18 @@ int ecf8_decode(const uint8_t* luts, const uint8_t* encoded,
                 int bytes_per_thread, void* cuda_stream);
 
 /*
- * Derives a stream's multi-symbol decode table (ECF8_TABLE_BYTES = 80 KB,
- * 16-byte aligned device memory: 8192 64-bit entries, one per 13-bit stream
- * prefix, each up to six whole symbols with their bit and symbol counts,
- * followed by one 16-bit mask of symbol start offsets per entry) from its
- * LUTs, asynchronously on cuda_stream.  The table depends on the LUTs
- * only, so it can be built once when a stream is loaded and passed in
- * ecf8_stream.table to every later decode; decodes without it derive the
- * table inside the kernel.  Corresponds to the per-block set-up the reference
- * loader does once (dfloat/run/run.py:453-458, shared_mem_size).
+ * Derives a stream's multi-symbol decode table (ECF8_TABLE_BYTES, 16-byte
+ * aligned device memory) from its LUTs, asynchronously on cuda_stream:
+ * 8192 64-bit entries, one per 13-bit stream prefix, each up to six whole
+ * symbols with their bit and symbol counts; one 16-bit mask of symbol start
+ * offsets per entry; a copy of the LUTs (18 rows, zero padded) and a 16-byte
+ * header.  The table depends on the LUTs only, so it can be built once when a
+ * stream is loaded and passed in ecf8_stream.table to every later decode.
+ * Every decode checks the stored LUT copy against the stream's LUTs and
+ * derives the table itself when they differ (or when no table is given), so
+ * a table built from other LUTs costs time but never correctness.
+ * Corresponds to the per-block set-up the reference loader does once
+ * (dfloat/run/run.py:453-458, shared_mem_size).
  */
 int ecf8_build_table(const uint8_t* luts, int n_luts, uint32_t* table,
                      void* cuda_stream);

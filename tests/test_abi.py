@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.ecf8_abi_version() == 6
+    assert lib.ecf8_abi_version() == 7
     assert lib.ecf8_status_string(0) == b"ok"
     assert b"invalid" in lib.ecf8_status_string(1)
     assert lib.ecf8_last_cuda_error() == 0

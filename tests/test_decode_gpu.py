@@ -331,6 +331,26 @@ def test_long_codes_everywhere(cuda_device, oracle_mod, seed):
         assert np.array_equal(run_reference_kernel(s, cuda_device), s["fp8"])
 
 
+TAB_LUT_OFF = 8192 * 8 + 8192 * 2  # prepared table: entries, end masks, LUT copy, header
+TAB_HDR_OFF = TAB_LUT_OFF + 18 * 256
+
+
+def test_stale_prepared_table_is_not_used(cuda_device, oracle_mod):
+    """A table built from another stream's LUTs (e.g. a cache keyed by a
+    reused address) is detected by its LUT copy: the kernel derives the
+    right table itself and the decode stays exact."""
+    from ecf8_b200.run import build_decode_table, decode_stream
+    rng = np.random.default_rng(77)
+    a = random_stream(oracle_mod, rng, n=200000, k=12)
+    b = random_stream(oracle_mod, rng, n=200000, k=5)
+    assert not np.array_equal(a["luts"], b["luts"]) or a["luts"].shape != b["luts"].shape
+    da, db = to_device(a, cuda_device), to_device(b, cuda_device)
+    stale = build_decode_table(db["luts"])
+    out = decode_stream(da["luts"], da["encoded"], da["packed_other_4bits"], da["output_positions"],
+                        da["gaps"], table=stale)
+    assert np.array_equal(out.view(torch.uint8).cpu().numpy(), a["fp8"])
+
+
 def test_corrupt_prepared_table_stays_in_bounds(cuda_device):
     """A table ecf8_build_table did not write (random words; random entries
     with in-range bit counts but more symbols than bits; random end masks)
@@ -350,6 +370,11 @@ def test_corrupt_prepared_table_stays_in_bounds(cuda_device):
             c = rng.integers(1, 7, 8192).astype(np.uint32)
             ent[:, 0] = (ent[:, 0] & 0xffffff00) | b
             ent[:, 1] = (b << 23) | (4 * c)
+        # A matching LUT copy and header, so the kernel takes the entries as they are.
+        tb = t.view(np.uint8)
+        tb[TAB_LUT_OFF:TAB_LUT_OFF + 18 * 256] = 0
+        tb[TAB_LUT_OFF:TAB_LUT_OFF + s["luts"].size] = s["luts"].reshape(-1)
+        tb[TAB_HDR_OFF:TAB_HDR_OFF + 8] = np.array([0x38464345, s["luts"].shape[0]], np.uint32).view(np.uint8)
         table = torch.from_numpy(t.view(np.int32).copy()).to(cuda_device)
         buf = torch.full((n + 64,), GUARD, dtype=torch.uint8, device=cuda_device)
         decode_stream(d["luts"], d["encoded"], d["packed_other_4bits"], d["output_positions"], d["gaps"],
