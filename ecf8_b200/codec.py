@@ -324,15 +324,14 @@ def encode_exponents_for_cuda(exponents_4bits, codec, bytes_per_thread=8, thread
     ex = exponents_4bits.reshape(-1).to(device=dev, dtype=torch.uint8).contiguous()
     n = ex.numel()
     bits, vals, eof_bits, eof_val = _code_arrays(codec)
-    present = torch.bincount(ex.long(), minlength=16)[:16].cpu().numpy() > 0
-    if np.any(present & (bits == 0)):
-        raise ValueError("an exponent that occurs has no code")
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
         ws = torch.empty(L.ecf8_encode_workspace_bytes(n), dtype=torch.uint8, device=dev)
         _lib.check(L.ecf8_encode_plan(ex.data_ptr(), n, bits.tobytes(), eof_bits, ws.data_ptr(), stream),
                    "ecf8_encode_plan")
-        total_bits, n_bytes, n_op = (int(x) for x in ws[-24:].view(torch.int64).cpu().tolist())
+        invalid, total_bits, n_bytes, n_op = (int(x) for x in ws[-32:].view(torch.int64).cpu().tolist())
+        if invalid:
+            raise ValueError(f"{invalid} exponents are above 15 or have no code")
         group = bytes_per_thread * threads_per_block
         grid = -(-n_bytes // group)
         cap = (n_bytes + 15) & ~15

@@ -76,24 +76,39 @@ __device__ __forceinline__ uint32_t sym_bits(const CodeTable& T, int s) {
     return s < 0 ? 0u : (uint32_t)T.bits[s & 15];
 }
 
-// Per-chunk code-length sums.
+// 1 for an exponent the code table cannot encode: a byte above 15 or a symbol
+// whose code length is 0.  Such exponents encode as nothing (their masked
+// length is 0), so every offset stays inside the planned stream; the plan
+// counts them and emit writes nothing when the count is not 0.
+__device__ __forceinline__ uint32_t sym_invalid(const CodeTable& T, int s) {
+    return s >= 0 && (s > 15 || T.bits[s & 15] == 0) ? 1u : 0u;
+}
+
+constexpr int kInvalidShift = 32;  // chunk sums: code bits in the low half, invalid exponents in the high half
+
+// Per-chunk code-length sums (low half) and invalid-exponent counts (high half).
 __global__ void __launch_bounds__(kThreads) chunk_bits_kernel(const uint8_t* __restrict__ ex, long long n,
                                                               const __grid_constant__ CodeTable T,
                                                               unsigned long long* __restrict__ chunk) {
     __shared__ uint32_t red[kThreads / 32];
+    __shared__ uint32_t red2[kThreads / 32];
     const long long i0 = (long long)blockIdx.x * kChunk + (long long)threadIdx.x * kPerThread;
     int sym[kPerThread];
     load16(ex, n, i0, sym);
-    uint32_t s = 0;
+    uint32_t s = 0, bad = 0;
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j) s += sym_bits(T, sym[j]);
+    for (int j = 0; j < kPerThread; ++j) {
+        s += sym_bits(T, sym[j]);
+        bad += sym_invalid(T, sym[j]);
+    }
     s = block_sum(s, red);
-    if (threadIdx.x == 0) chunk[blockIdx.x] = s;
+    bad = block_sum(bad, red2);
+    if (threadIdx.x == 0) chunk[blockIdx.x] = (unsigned long long)s | ((unsigned long long)bad << kInvalidShift);
 }
 
 // Exclusive scan of the chunk sums in place (chunk[c] becomes the first bit of
-// chunk c) and the stream plan: plan[0] total bits, plan[1] encoded bytes,
-// plan[2] output_positions entries.
+// chunk c) and the stream plan: plan[-1] invalid exponents, plan[0] total bits,
+// plan[1] encoded bytes, plan[2] output_positions entries.
 __global__ void __launch_bounds__(kScanThreads) scan_plan_kernel(const uint8_t* __restrict__ ex, long long n,
                                                                  const __grid_constant__ CodeTable T,
                                                                  unsigned long long* __restrict__ chunk,
@@ -101,12 +116,15 @@ __global__ void __launch_bounds__(kScanThreads) scan_plan_kernel(const uint8_t* 
                                                                  unsigned long long* __restrict__ plan) {
     __shared__ unsigned long long wsum[kScanThreads / 32];
     __shared__ unsigned long long carry;
-    if (threadIdx.x == 0) carry = 0;
+    __shared__ unsigned long long invalid;
+    if (threadIdx.x == 0) carry = invalid = 0;
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     for (long long b = 0; b < n_chunks; b += kScanThreads) {
         const long long i = b + threadIdx.x;
-        const unsigned long long x = i < n_chunks ? chunk[i] : 0ull;
+        const unsigned long long raw = i < n_chunks ? chunk[i] : 0ull;
+        const unsigned long long x = raw & 0xffffffffull;
+        if (raw >> kInvalidShift) atomicAdd(&invalid, raw >> kInvalidShift);
         unsigned long long v = x;
         for (int o = 1; o < 32; o <<= 1) {
             const unsigned long long y = __shfl_up_sync(0xffffffffu, v, o);
@@ -140,6 +158,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_plan_kernel(const uint8_t* 
             n_op += last_start / kGroupBits + 1;
             if ((total % 8) && total / kGroupBits > last_start / kGroupBits) n_op += 1;  // utils.py:444-445
         }
+        plan[-1] = invalid;
         plan[0] = total;
         plan[1] = n_bytes;
         plan[2] = n_op;
@@ -198,6 +217,7 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(const uint8_t* __restric
     }
     __syncthreads();
     const unsigned long long total = chunk[gridDim.x];
+    if (chunk[gridDim.x + 1]) return;  // the plan counted invalid exponents: no stream
     const unsigned long long b0 = chunk[c] + (v - local) + (warp ? wsum[warp - 1] : 0u);
     if (local == 0) return;
 
@@ -218,8 +238,8 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(const uint8_t* __restric
 #pragma unroll
     for (int j = 0; j < kPerThread; ++j) {
         if (sym[j] < 0) break;
-        const uint32_t len = T.bits[sym[j]];
-        const uint32_t code = T.val[sym[j]];
+        const uint32_t len = T.bits[sym[j] & 15];
+        const uint32_t code = T.val[sym[j] & 15];
         const long long i = i0 + j;
         // window / group bookkeeping (utils.py:392-406)
         const unsigned long long ps = (j == 0) ? prev_start : last_start;
@@ -295,26 +315,28 @@ int make_table(const uint8_t* code_bits, const uint32_t* code_values, int eof_bi
 }
 
 // --- No-allocation variant --------------------------------------------------
-// Chunk bit offsets (+ total) and the 3-entry plan for streams of up to
-// kStaticMaxChunks chunks live in this file-scope array instead of a
-// caller-provided workspace.  One copy per GPU that loads the library,
-// held until the process exits.
+// Chunk bit offsets (+ total), the invalid-exponent count and the 3-entry
+// plan for streams of up to kStaticMaxChunks chunks live in this file-scope
+// array instead of a caller-provided workspace.  One copy per GPU that loads
+// the library, held until the process exits.
 constexpr long long kStaticMaxChunks = 65536;  // 65536 x 4096 = 268,435,456 elements
 static_assert((long long)ECF8_NOALLOC_MAX_ELEMENTS == kStaticMaxChunks * kChunk, "limit mismatch");
-__device__ __align__(256) unsigned long long g_static_scratch[kStaticMaxChunks + 1 + 3];
+static __device__ __align__(256) unsigned long long g_static_scratch[kStaticMaxChunks + 1 + 1 + 3];
 
 constexpr int kMaxDevices = 64;
-std::once_flag g_scratch_once[kMaxDevices];
+std::mutex g_scratch_mutex;
+bool g_scratch_ready[kMaxDevices];
 void* g_scratch_ptr[kMaxDevices];
-int g_scratch_status[kMaxDevices];
 
-// Writes the trailing output position from the plan the same launch sequence computed.
+// Writes the trailing output position from the plan the same launch sequence
+// computed (nothing when the plan counted invalid exponents).
 __global__ void op_tail_from_plan_kernel(uint64_t* op, const unsigned long long* plan, long long n) {
-    op[plan[2] - 1] = (uint64_t)n;
+    if (plan[-1] == 0) op[plan[2] - 1] = (uint64_t)n;
 }
 
+// sizes = the plan, or {0, 0, 0} when it counted invalid exponents.
 __global__ void copy_plan_kernel(uint64_t* sizes, const unsigned long long* plan) {
-    if (threadIdx.x < 3) sizes[threadIdx.x] = plan[threadIdx.x];
+    if (threadIdx.x < 3) sizes[threadIdx.x] = plan[-1] ? 0ull : plan[threadIdx.x];
 }
 
 }  // namespace
@@ -325,7 +347,7 @@ extern "C" {
 int64_t ecf8_encode_workspace_bytes(int64_t n) {
     if (n < 0) return -1;
     const int64_t chunks = (n + ecf8enc::kChunk - 1) / ecf8enc::kChunk;
-    return (chunks + 1 + 3) * 8;  // chunk starts + total, then the 3-entry plan
+    return (chunks + 1 + 1 + 3) * 8;  // chunk starts + total, invalid-exponent count, the 3-entry plan
 }
 
 int ecf8_encode_plan(const uint8_t* exponents, int64_t n, const uint8_t* code_bits, int eof_bits,
@@ -339,7 +361,7 @@ int ecf8_encode_plan(const uint8_t* exponents, int64_t n, const uint8_t* code_bi
     cudaStream_t s = (cudaStream_t)cuda_stream;
     const long long chunks = (n + kChunk - 1) / kChunk;
     unsigned long long* chunk = reinterpret_cast<unsigned long long*>(workspace);
-    unsigned long long* plan = chunk + chunks + 1;
+    unsigned long long* plan = chunk + chunks + 2;
     if (chunks > 0x7fffffffLL) return ECF8_ERR_INVALID_ARGUMENT;
     if (chunks > 0) chunk_bits_kernel<<<(unsigned)chunks, kThreads, 0, s>>>(exponents, n, T, chunk);
     scan_plan_kernel<<<1, kScanThreads, 0, s>>>(exponents, n, T, chunk, chunks, plan);
@@ -419,16 +441,22 @@ int ecf8_encode_noalloc(const uint8_t* exponents, int64_t n, const uint8_t* code
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return cuda_fail(e);
     if (dev < 0 || dev >= kMaxDevices) return ECF8_ERR_UNSUPPORTED;
-    std::call_once(g_scratch_once[dev], [dev]() {
-        void* ptr = nullptr;
-        cudaError_t err = cudaGetSymbolAddress(&ptr, g_static_scratch);
-        g_scratch_status[dev] = (int)err;
-        g_scratch_ptr[dev] = ptr;
-    });
-    if (g_scratch_status[dev] != cudaSuccess) return cuda_fail((cudaError_t)g_scratch_status[dev]);
-    unsigned long long* chunk = static_cast<unsigned long long*>(g_scratch_ptr[dev]);
+    // A failed lookup is not remembered: the next call on the device tries again.
+    void* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_scratch_mutex);
+        if (!g_scratch_ready[dev]) {
+            void* ptr = nullptr;
+            cudaError_t err = cudaGetSymbolAddress(&ptr, g_static_scratch);
+            if (err != cudaSuccess) return cuda_fail(err);
+            g_scratch_ptr[dev] = ptr;
+            g_scratch_ready[dev] = true;
+        }
+        base = g_scratch_ptr[dev];
+    }
+    unsigned long long* chunk = static_cast<unsigned long long*>(base);
     const long long chunks = (n + kChunk - 1) / kChunk;
-    unsigned long long* plan = chunk + chunks + 1;
+    unsigned long long* plan = chunk + chunks + 2;
     cudaStream_t s = (cudaStream_t)cuda_stream;
     // The scratch keeps the previous call's values; every entry this call
     // reads (chunk sums, their scan, the plan) is rewritten below before it is

@@ -21,6 +21,7 @@ import math
 import os
 import re
 import threading
+from collections import OrderedDict
 from sys import stderr
 from typing import Dict, Optional, Union
 
@@ -201,15 +202,48 @@ class _DecodeLauncher:
     Called like the reference launch: ``_decode(grid=(G,), block=(512,),
     shared_mem=S, args=[luts, encoded, packed_other_4bits, output_positions,
     gaps, outputs, n_luts, n_bytes, n_elements])`` where the six buffers are
-    device pointers (ints) or tensors.  grid / block must be the reference
-    geometry (G = ceil(n_bytes / 4096), 512 threads); shared_mem is accepted
-    and ignored (the engine sizes its own).  Like the reference it launches
-    asynchronously on the current stream and returns nothing; unlike it, a
-    bad argument raises.  output_positions is read for the first G entries
-    only (the trailing entry is always n_elements), so a short array is safe.
+    device pointers (ints) or tensors on the current device.  grid / block
+    must be the reference geometry (G = ceil(n_bytes / 4096), 512 threads);
+    shared_mem is accepted and ignored (the engine sizes its own).  Like the
+    reference it launches asynchronously on the current stream and returns
+    nothing; unlike it, a bad argument raises.  output_positions is read for
+    the first G entries only (the trailing entry is always n_elements), so a
+    short array is safe.
+
+    The multi-symbol decode table is built once per (device, luts address,
+    n_luts) and kept in a small cache (`cache_size` tables of
+    ECF8_TABLE_BYTES each), so repeated calls on a block do not derive it in
+    every CTA of every launch.  The kernel compares each cached table's copy
+    of the LUTs with the LUTs it is given and derives the table itself when
+    they differ, so a cached table whose LUT memory was reused for other LUTs
+    only costs that derivation; ``clear_cache()`` drops every cached table.
     """
 
     bytes_per_thread = 8
+    cache_size = 256
+
+    def __init__(self):
+        self._tables = OrderedDict()
+        self._lock = threading.Lock()
+
+    def clear_cache(self):
+        with self._lock:
+            self._tables.clear()
+
+    def _table(self, luts_ptr, n_luts, device, cuda_stream):
+        key = (device.index, luts_ptr, n_luts)
+        with self._lock:
+            t = self._tables.get(key)
+            if t is not None:
+                self._tables.move_to_end(key)
+                return t
+        t = torch.empty(_lib.TABLE_BYTES // 4, dtype=torch.int32, device=device)
+        _lib.check(_lib.lib().ecf8_build_table(luts_ptr, n_luts, t.data_ptr(), cuda_stream), "_decode table")
+        with self._lock:
+            self._tables[key] = t
+            while len(self._tables) > self.cache_size:
+                self._tables.popitem(last=False)
+        return t
 
     def __call__(self, grid, block, args, shared_mem=0, stream=None):
         if len(args) != 9:
@@ -222,11 +256,17 @@ class _DecodeLauncher:
         want = math.ceil(n_bytes / (tpb * self.bytes_per_thread))
         if g != want:
             raise ValueError(f"grid {g} does not cover {n_bytes} bytes (expected {want})")
+        device = torch.device("cuda", torch.cuda.current_device())
         if stream is None:
-            stream = torch.cuda.current_stream()
+            stream = torch.cuda.current_stream(device)
         cuda_stream = stream.cuda_stream if hasattr(stream, "cuda_stream") else int(stream or 0)
-        st = _lib.lib().ecf8_decode(*ptrs, n_luts, n_bytes, n_elements, max(g, 1), g * tpb // 2,
-                                    tpb, self.bytes_per_thread, cuda_stream)
+        table = None
+        if 2 <= n_luts <= _lib.MAX_LUTS and ptrs[0] and n_elements > 0:
+            table = self._table(ptrs[0], n_luts, device, cuda_stream)
+        arr = (_lib.Ecf8Stream * 1)(_lib.Ecf8Stream(
+            ptrs[0], n_luts, 0, ptrs[1], n_bytes, ptrs[2], ptrs[3], max(g, 1), ptrs[4], g * tpb // 2, ptrs[5],
+            n_elements, table.data_ptr() if table is not None else None))
+        st = _lib.lib().ecf8_decode_batch(arr, 1, tpb, self.bytes_per_thread, cuda_stream)
         _lib.check(st, "_decode")
 
 
@@ -356,13 +396,6 @@ def _load_one(model, tensor_name, tensor_value, params, buffers, state_keys, pat
                                    pattern_dict, tpb, bpt)
 
 
-def _order_for_load(tensors):
-    # `encoded` must come after nothing in particular, but output_positions
-    # must be registered before its shared-memory size is computed: it is
-    # computed from the buffer itself, so file order is fine.
-    return tensors.items()
-
-
 def load_and_replace_tensors(model, directory_path, dfloat_config):
     """Loads every .safetensors file of a compressed checkpoint into `model`
     (run.py:158-275): known parameters/buffers are replaced, ECF8 buffers are
@@ -377,7 +410,7 @@ def load_and_replace_tensors(model, directory_path, dfloat_config):
         params = dict(model.named_parameters())
         buffers = dict(model.named_buffers())
         keys = set(model.state_dict().keys())
-        for tname, tval in _order_for_load(tensors):
+        for tname, tval in tensors.items():
             _load_one(model, tname, tval, params, buffers, keys, pattern_dict, tpb, bpt)
     return model
 
@@ -403,7 +436,7 @@ def load_and_replace_tensors_parallel(model, directory_path, dfloat_config):
             print(f"Error loading {name}: {e}", file=stderr)
             return 0
         with lock:  # module registration mutates the model
-            for tname, tval in _order_for_load(tensors):
+            for tname, tval in tensors.items():
                 _load_one(model, tname, tval, params, buffers, keys, pattern_dict, tpb, bpt)
         return len(tensors)
 
@@ -445,7 +478,9 @@ def report_model_size(model, include_pattern):
     return inc / gb, exc / gb, (inc + exc) / gb
 
 
-def _no_split_classes(model, patterns):
+def get_no_split_classes(model, patterns):
+    """Class names of the modules whose full name matches one of `patterns`
+    (run.py:461-470): the blocks accelerate must not split across devices."""
     out = []
     for name, m in model.named_modules():
         if any(re.fullmatch(p, name) for p in patterns):
@@ -524,7 +559,7 @@ class DFloatModel:
             except ImportError:
                 model = model.to(torch.device("cuda", torch.cuda.current_device()))
             else:
-                classes = _no_split_classes(model, get_default_no_split_pattern(model.__class__.__name__))
+                classes = get_no_split_classes(model, get_default_no_split_pattern(model.__class__.__name__))
                 mm = get_balanced_memory(model, max_memory=max_memory, no_split_module_classes=classes)
                 dm = infer_auto_device_map(model, max_memory=mm, no_split_module_classes=classes)
                 model = dispatch_model(model, dm)

@@ -148,12 +148,17 @@ int ecf8_decode_batch_flags(const ecf8_stream* streams, int n_streams,
  * (host) the code length of each symbol (0 = symbol absent).  workspace must
  * hold ecf8_encode_workspace_bytes(n) bytes of device memory.  Writes into
  * its last three u64 (device memory) the total bit count, the encoded byte
- * count and the number of output_positions entries the stream will have.
+ * count and the number of output_positions entries the stream will have, and
+ * into the u64 before them the number of invalid exponents: bytes above 15 or
+ * symbols whose code length is 0.  The stream exists only when that count is
+ * 0 (the reference packer fails on such input: dfloat/utils.py:408 looks the
+ * symbol up in the code table).
  *
  * ecf8_encode_emit: same exponents / code table plus code values and the EOF
  * code; writes encoded (capacity >= round-up of n_bytes to 4 bytes), gaps
  * (n_gap_bytes = ceil(n_bytes/4096) * 256) and output_positions (the count the
- * plan reported).  The three output buffers are cleared by the call.
+ * plan reported).  The three output buffers are cleared by the call; when the
+ * plan counted invalid exponents nothing else is written.
  */
 int64_t ecf8_encode_workspace_bytes(int64_t n);
 int ecf8_encode_plan(const uint8_t* exponents, int64_t n,
@@ -193,7 +198,9 @@ int ecf8_encode_emit(const uint8_t* exponents, int64_t n,
  * count + 2 entries.  sizes (3 u64, device) receives the total bit count, the
  * encoded byte count and the number of output_positions entries; the buffers
  * equal ecf8_encode_emit()'s for the same input up to those sizes (gaps up to
- * ceil(n_bytes/4096)*256 bytes).  Asynchronous on cuda_stream.
+ * ceil(n_bytes/4096)*256 bytes).  An exponent above 15, or one whose symbol
+ * has code length 0, makes sizes {0, 0, 0} and leaves the outputs cleared.
+ * Asynchronous on cuda_stream.
  */
 #define ECF8_NOALLOC_MAX_ELEMENTS 268435456LL
 int ecf8_encode_noalloc(const uint8_t* exponents, int64_t n,

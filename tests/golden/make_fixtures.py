@@ -1,9 +1,8 @@
 """Generates the golden ECF8 streams under tests/golden/ from the REFERENCE codec.
 
-Run in a container that has the reference checkout (default
-/root/reference, or $ECF8_REFERENCE_DIR):
+Run where a reference checkout exists, named by ECF8_REFERENCE_DIR:
 
-    python tests/golden/make_fixtures.py
+    ECF8_REFERENCE_DIR=/path/to/ecf8 python tests/golden/make_fixtures.py
 
 It imports the reference's own ``dfloat/utils.py`` (with the test-only
 ``oracle/dahuffman.py`` stand-in for the missing third-party ``dahuffman``)
@@ -31,7 +30,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("ECF8_REFERENCE_DIR", "/root/reference")
+REF = os.environ.get("ECF8_REFERENCE_DIR")
+if not REF or not os.path.isfile(os.path.join(REF, "dfloat", "utils.py")):
+    sys.exit("make_fixtures.py: set ECF8_REFERENCE_DIR to a zeyuyang8/ecf8 checkout")
 sys.path.insert(0, os.path.join(REPO, "oracle"))  # dahuffman stand-in
 sys.path.insert(0, REF)
 

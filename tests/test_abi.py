@@ -85,9 +85,10 @@ def test_batch_rejects_bad_arguments(lib):
 
 
 def test_encode_workspace_size(lib):
-    assert lib.ecf8_encode_workspace_bytes(0) == 32
-    assert lib.ecf8_encode_workspace_bytes(4096) == 40
-    assert lib.ecf8_encode_workspace_bytes(4097) == 48
+    # chunk starts + total, the invalid-exponent count, the 3-entry plan
+    assert lib.ecf8_encode_workspace_bytes(0) == 40
+    assert lib.ecf8_encode_workspace_bytes(4096) == 48
+    assert lib.ecf8_encode_workspace_bytes(4097) == 56
     assert lib.ecf8_encode_workspace_bytes(-1) == -1
 
 

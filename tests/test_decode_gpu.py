@@ -423,3 +423,34 @@ def test_overlap_previous_batched_matches_plain(cuda_device):
         torch.cuda.synchronize()
         for s, o in zip(ss, outs):
             assert np.array_equal(o.cpu().numpy(), s["fp8"])
+
+
+def test_overlap_previous_waits_for_a_long_kernel_writing_the_outputs(cuda_device):
+    """The overlapped decode must not write before the previous kernel has
+    completed.  The previous kernel here is a long decode (64 M elements, tens
+    of microseconds) of another stream into a buffer that contains the
+    overlapped decode's output region; if the second decode wrote early, the
+    first would overwrite part of its bytes."""
+    from ecf8_b200.codec import compress_fp8
+    from ecf8_b200.run import build_decode_table, decode_stream
+    g = torch.Generator(device=cuda_device).manual_seed(4)
+    n_big = 64 << 20
+    big = (torch.randn(n_big, generator=g, device=cuda_device) * 20).to(torch.float8_e4m3fn)
+    c = compress_fp8(big)
+    tb = build_decode_table(c["luts"])
+    buf = torch.empty(n_big, dtype=torch.uint8, device=cuda_device)
+    for i, name in enumerate(golden_names()):
+        s = load_golden(name)
+        d = to_device(s, cuda_device)
+        t = build_decode_table(d["luts"])
+        n = s["fp8"].size
+        off = (n_big - n) // 2 if i % 2 else n_big - n - 16 * i
+        torch.cuda.synchronize()
+        decode_stream(c["luts"], c["encoded"], c["packed_other_4bits"], c["output_positions"], c["gaps"], buf,
+                      table=tb)
+        decode_stream(d["luts"], d["encoded"], d["packed_other_4bits"], d["output_positions"], d["gaps"],
+                      buf[off:off + n], table=t, overlap_previous=True)
+        torch.cuda.synchronize()
+        assert np.array_equal(buf[off:off + n].cpu().numpy(), s["fp8"]), name
+        ref = big.view(torch.uint8)
+        assert torch.equal(buf[:off], ref[:off]) and torch.equal(buf[off + n:], ref[off + n:])

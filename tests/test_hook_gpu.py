@@ -104,3 +104,60 @@ def test_hooked_model_matches_uncompressed(cuda_device, tmp_path, parallel):
     ptrs = {blk.down_proj.weight.data_ptr() for blk in model.layers}
     assert len(ptrs) == 1
     assert TensorManager._tensors[dev].numel() == 3 * 256 * 512
+
+
+def test_hooked_model_through_the_dfloat_import_path(cuda_device, tmp_path):
+    """The same round trip with the reference's import path only
+    (``from dfloat.run import ...``, ``from dfloat.run.run import TensorManager``)."""
+    from dfloat.run import load_and_replace_tensors_parallel
+    from dfloat.run.run import TensorManager
+    dev = cuda_device
+    ref = Tiny(dev)
+    x = torch.randn(8, 256, device=dev)
+    y_ref = ref(x)
+    save_compressed(ref, str(tmp_path))
+    model = Tiny(dev, seed=7)
+    cfg = {"threads_per_block": 512, "bytes_per_thread": 8,
+           "pattern_dict": json.load(open(tmp_path / "pattern_dict.json"))}
+    load_and_replace_tensors_parallel(model, str(tmp_path), cfg)
+    model.to(dev)
+    TensorManager.clear_device()
+    for _ in range(3):
+        assert torch.equal(model(x), y_ref)
+
+
+def test_reference_launcher_caches_tables_and_survives_reused_lut_memory(cuda_device):
+    """`_decode` with the reference's call convention (compress.py:109-124):
+    the first call on a LUT address builds a table, later calls reuse it; new
+    LUTs written to the same address are detected by the kernel, so the decode
+    stays exact, and clear_cache() drops the tables."""
+    import numpy as np
+    import sys
+    sys.path.insert(0, os.path.join(os.path.dirname(__file__)))
+    from conftest import load_golden
+    from helpers import to_device
+    from dfloat.run import _decode
+    a, b = load_golden("gauss_per_tensor"), load_golden("fibonacci_depth16")
+    luts = torch.zeros(18, 256, dtype=torch.uint8, device=cuda_device)
+
+    def run(s):
+        d = to_device(s, cuda_device)
+        n_l = s["luts"].shape[0]
+        luts[:n_l] = d["luts"]
+        n = s["fp8"].size
+        out = torch.zeros(n, dtype=torch.uint8, device=cuda_device)
+        grid = (-(-d["encoded"].numel() // 4096),)
+        _decode(grid=grid, block=(512,), shared_mem=0,
+                args=[luts.data_ptr(), d["encoded"].data_ptr(), d["packed_other_4bits"].data_ptr(),
+                      d["output_positions"].data_ptr(), d["gaps"].data_ptr(), out.data_ptr(), n_l,
+                      d["encoded"].numel(), n])
+        torch.cuda.synchronize()
+        return np.array_equal(out.cpu().numpy(), s["fp8"])
+
+    _decode.clear_cache()
+    assert run(a) and run(a)
+    assert len(_decode._tables) == 1
+    assert run(b)  # other LUTs at the same address (same n_luts or not): still exact
+    assert run(a)
+    _decode.clear_cache()
+    assert not _decode._tables

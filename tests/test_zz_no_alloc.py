@@ -81,3 +81,42 @@ def test_noalloc_packer_rejects_streams_beyond_its_scratch(cuda_device):
     st = L.ecf8_encode_noalloc(16, n, bits, vals, 2, 3, 16, 1 << 40, 16, 1 << 40, 16, 1 << 30, 16, None)
     assert st == _lib.ERR_TOO_LARGE
     assert b"268,435,456" in L.ecf8_status_string(st)
+
+
+def test_noalloc_packer_rejects_invalid_exponents_on_the_device(cuda_device):
+    """Exponent bytes above 15 (or symbols without a code) are found on the
+    device: sizes come back {0, 0, 0}, the outputs stay cleared and nothing
+    outside them is written.  A valid call right after works as before."""
+    from ecf8_b200 import _lib
+    L = _lib.lib()
+    rng = np.random.default_rng(8)
+    bits = np.zeros(16, np.uint8)
+    bits[:4] = [1, 2, 3, 3]
+    vals = (ctypes.c_uint32 * 16)(*([0, 2, 6, 7] + [0] * 12))
+    e = torch.from_numpy(rng.integers(0, 4, 20000).astype(np.uint8)).to(cuda_device)
+    e[123] = 77
+    n = e.numel()
+    max_bytes = -(-n * 3 // 8)
+    groups = -(-max_bytes // 4096)
+    guard = 64
+    enc = torch.full(((max_bytes + 3) & ~3) + 2 * guard, 0xA5, dtype=torch.uint8, device=cuda_device)
+    gaps = torch.full((groups * 256 + 2 * guard,), 0xA5, dtype=torch.uint8, device=cuda_device)
+    op = torch.full((groups + 2 + 16,), -1, dtype=torch.int64, device=cuda_device)
+    sizes = torch.full((3,), -1, dtype=torch.int64, device=cuda_device)
+    st = torch.cuda.current_stream(cuda_device).cuda_stream
+    r = L.ecf8_encode_noalloc(e.data_ptr(), n, bits.tobytes(), vals, 4, 15, enc[guard:].data_ptr(),
+                              enc.numel() - 2 * guard, gaps[guard:].data_ptr(), gaps.numel() - 2 * guard,
+                              op[8:].data_ptr(), groups + 2, sizes.data_ptr(), st)
+    assert r == 0
+    torch.cuda.synchronize()
+    assert sizes.cpu().tolist() == [0, 0, 0]
+    assert not enc[guard:-guard].any() and torch.all(enc[:guard] == 0xA5) and torch.all(enc[-guard:] == 0xA5)
+    assert not gaps[guard:-guard].any() and torch.all(gaps[:guard] == 0xA5) and torch.all(gaps[-guard:] == 0xA5)
+    assert not op[8:8 + groups + 2].any() and torch.all(op[:8] == -1) and torch.all(op[8 + groups + 2:] == -1)
+    e[123] = 1
+    table = {s: (int(bits[s]), int(vals[s])) for s in range(4)}
+    from ecf8_b200.codec import EOF
+    table[EOF] = (4, 15)
+    got = noalloc_pack(e, table, cuda_device)
+    torch.cuda.synchronize()
+    assert got[3].cpu().tolist()[1] > 0
