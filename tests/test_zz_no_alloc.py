@@ -99,7 +99,7 @@ def test_noalloc_packer_rejects_invalid_exponents_on_the_device(cuda_device):
     max_bytes = -(-n * 3 // 8)
     groups = -(-max_bytes // 4096)
     guard = 64
-    enc = torch.full(((max_bytes + 3) & ~3) + 2 * guard, 0xA5, dtype=torch.uint8, device=cuda_device)
+    enc = torch.full((((max_bytes + 3) & ~3) + 2 * guard,), 0xA5, dtype=torch.uint8, device=cuda_device)
     gaps = torch.full((groups * 256 + 2 * guard,), 0xA5, dtype=torch.uint8, device=cuda_device)
     op = torch.full((groups + 2 + 16,), -1, dtype=torch.int64, device=cuda_device)
     sizes = torch.full((3,), -1, dtype=torch.int64, device=cuda_device)
