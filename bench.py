@@ -3,17 +3,21 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ecf8|reference]
 
-N = 1 (default): config 2, the Qwen3-8B-shaped FP8 weight set: 36 layers,
-each one ECF8 stream of q/k/v/o/gate/up/down (192,937,984 e4m3 weights,
-sub-Linears concatenated in sorted-name order as the reference compressor
-does), N(0, 0.02) weights with 128x128 block scales, seed layer*7 + index.
-A step decodes every layer once into the per-device scratch buffer, one
-C-ABI launch per layer, exactly as the decode-before-forward hook does.
+Plain `python bench.py` (N = 1): config 2, the Qwen3-8B-shaped FP8 weight
+set: 36 layers, each one ECF8 stream of q/k/v/o/gate/up/down (192,937,984
+e4m3 weights, sub-Linears concatenated in sorted-name order as the reference
+compressor does), N(0, 0.02) weights with 128x128 block scales, seed
+layer*7 + index.  A step decodes every layer once into the per-device
+scratch buffer, one C-ABI launch per layer, exactly as the
+decode-before-forward hook does.
 
-N > 1 (under torchrun, one rank per GPU): config 5, the Qwen3-235B-A22B-shaped
-MoE weight set.  Experts are partitioned evenly across ranks; each rank
-decodes, per layer, its own experts plus its replica of the attention stream
-with one batched launch.  No collective touches the data path.
+Under torchrun (one rank per GPU, any world size including 1): config 5, the
+Qwen3-235B-A22B-shaped MoE weight set, --moe-layers layers (default 48, so
+that the N = 1 shard fits one B200).  All 128 experts of every layer are
+partitioned evenly across ranks; each rank decodes, per layer, its own
+experts plus its replica of the attention stream with one batched launch.
+No collective touches the data path.  The same workload at every N makes
+the 1 -> 8 curve comparable.
 
 --impl reference: the reference's CPU decode (the oracle's C restatement of
 dfloat/run/decode.cu, all host threads) on a bounded sample of the same
@@ -49,6 +53,7 @@ QWEN3_235B_ATTN = [("k_proj", 512, 4096), ("o_proj", 4096, 8192), ("q_proj", 819
 QWEN3_235B_EXPERT = [("down_proj", 4096, 1536), ("gate_proj", 1536, 4096), ("up_proj", 1536, 4096)]
 QWEN3_235B_LAYERS = 94
 QWEN3_235B_EXPERTS = 128
+MOE_BENCH_LAYERS = 48  # config-5 layers a bench step decodes: the N = 1 shard (~104 GB) fits one B200
 FALLBACK_HBM_GBS = 6650.0
 L2_BYTES = 126 * 2 ** 20
 
@@ -213,17 +218,35 @@ def build_qwen3_8b(dev, n_layers=QWEN3_8B_LAYERS):
     return layers, originals
 
 
-def build_moe(dev, rank, world, n_layers):
-    from ecf8_b200.codec import compress_fp8
-    from ecf8_b200.run import build_decode_table
+def moe_plan(rank, world, n_layers):
+    """Config-5 sharding: (owned experts, per-layer stream list) of one rank.
+    Rank r owns experts [r * 128/N, (r+1) * 128/N) of every layer and a replica
+    of the layer's attention stream; each stream is (name, seed of its first
+    Linear, Linear shapes), the attention stream first."""
+    if world < 1 or QWEN3_235B_EXPERTS % world:
+        raise ValueError(f"{QWEN3_235B_EXPERTS} experts do not split evenly over {world} ranks")
     per = QWEN3_235B_EXPERTS // world
     owned = list(range(rank * per, (rank + 1) * per))
     layers = []
-    t0 = time.time()
     for l in range(n_layers):
-        streams = [compress_fp8(make_stream_weights(QWEN3_235B_ATTN, (l * 1000 + 999) * 10, dev))]
-        for e in owned:
-            streams.append(compress_fp8(make_stream_weights(QWEN3_235B_EXPERT, (l * 1000 + e) * 10, dev)))
+        ly = [(f"model.layers.{l}.self_attn", (l * 1000 + 999) * 10, QWEN3_235B_ATTN)]
+        ly += [(f"model.layers.{l}.mlp.experts.{e}", (l * 1000 + e) * 10, QWEN3_235B_EXPERT) for e in owned]
+        layers.append(ly)
+    return owned, layers
+
+
+def plan_elements(layers):
+    return sum(o * i for ly in layers for _, _, shapes in ly for _, o, i in shapes)
+
+
+def build_moe(dev, rank, world, n_layers):
+    from ecf8_b200.codec import compress_fp8
+    from ecf8_b200.run import build_decode_table
+    owned, plan = moe_plan(rank, world, n_layers)
+    layers = []
+    t0 = time.time()
+    for ly in plan:
+        streams = [compress_fp8(make_stream_weights(shapes, seed, dev)) for _, seed, shapes in ly]
         for c in streams:
             c["decode_table"] = build_decode_table(c["luts"])
         layers.append(streams)
@@ -243,12 +266,124 @@ def decode_args(L, c, out, stream):
     return (arr, 1, 512, 8, _lib.DECODE_OVERLAP_PREVIOUS, stream.cuda_stream)
 
 
+def under_torchrun():
+    """True when launched by torch.distributed.run (at any world size)."""
+    return "TORCHELASTIC_RUN_ID" in os.environ or "LOCAL_WORLD_SIZE" in os.environ
+
+
+def pick_workload(args):
+    if args.workload != "auto":
+        return args.workload
+    return "config5" if under_torchrun() else "config2"
+
+
+def timed_steps(step, k, stream, world, dev):
+    """k steps between a barrier + synchronisation on both sides, timed with
+    CUDA events on the launching stream; returns (ms per step, max over ranks;
+    this rank's ms for all k steps; clock summary)."""
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clk:
+        t_start.record(stream)
+        for _ in range(k):
+            step()
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_total = t_start.elapsed_time(t_end)
+    return max_over_ranks(ms_total / k, world), ms_total, clk.summary()
+
+
+def call_convention_times(L, c, scratch, stream, reps=20):
+    """Per-launch device time of one layer stream through three entry points,
+    each launch ordered after the previous one (no overlap): the prepared
+    table (what the hook passes), the reference's `_decode(grid=, block=,
+    args=[...])` convention (its table cache built on the first call), and
+    ecf8_decode without a table (every CTA derives it)."""
+    from ecf8_b200 import _lib
+    from ecf8_b200.run import _decode, _stream_struct
+    n = c["packed_other_4bits"].numel() * 2
+    arr = (_lib.Ecf8Stream * 1)(_stream_struct(c, scratch, c["decode_table"]))
+    grid = (-(-c["encoded"].numel() // 4096),)
+    ptrs = [c["luts"].data_ptr(), c["encoded"].data_ptr(), c["packed_other_4bits"].data_ptr(),
+            c["output_positions"].data_ptr(), c["gaps"].data_ptr(), scratch.data_ptr()]
+    n_op = c["output_positions"].numel()
+    paths = {
+        "prepared_table": lambda: L.ecf8_decode_batch(arr, 1, 512, 8, stream.cuda_stream),
+        "reference_convention_decode": lambda: _decode(grid=grid, block=(512,), shared_mem=0,
+                                                       args=ptrs + [c["luts"].shape[0], c["encoded"].numel(), n]),
+        "no_table_ecf8_decode": lambda: L.ecf8_decode(*ptrs, c["luts"].shape[0], c["encoded"].numel(), n, n_op,
+                                                      c["gaps"].numel(), 512, 8, stream.cuda_stream),
+    }
+    out = {}
+    for name, fn in paths.items():
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            fn()
+        b.record(stream)
+        torch.cuda.synchronize()
+        out[name + "_us"] = round(a.elapsed_time(b) / reps * 1e3, 2)
+    out["what"] = (f"one Qwen3-8B layer stream ({n:,} weights), {reps} launches each, ordered one after "
+                   "another; _decode keeps one prepared table per LUT address")
+    return out
+
+
+def run_generation(args, dev):
+    """Config 3, bounded: the full random-init Qwen3-8B architecture (36
+    layers, FP8 Linears with 128x128 block scales), batch 16 x 128 random
+    prompt ids, --gen-tokens greedy new tokens; the uncompressed FP8 model,
+    then the same model with every decoder layer ECF8-compressed in place and
+    decoded by the forward-pre-hook.  Each arm first runs one untimed
+    generation of the same length; the timed one is between two
+    synchronisations (inference_llm.py:109-160 of the reference).  Both arms
+    use the same block-scaled FP8 GEMM, which reads e4m3 weights directly."""
+    from ecf8_b200 import fp8_model
+    from ecf8_b200.compress import compress_model_in_place
+    from ecf8_b200.inference_llm import generate_timed, qwen3_8b_config
+    from ecf8_b200.run import TensorManager
+    t0 = time.time()
+    model = fp8_model.fp8_model_from_config(qwen3_8b_config(QWEN3_8B_LAYERS), device=dev, seed=42)
+    g = torch.Generator(device=dev).manual_seed(42)
+    ids = torch.randint(0, model.config.vocab_size, (16, 128), generator=g, device=dev)
+    n = args.gen_tokens
+    unc, tok_u, sums_u, full_u = generate_timed(model, ids, n, keep=2, warm_tokens=n)
+    compress_model_in_place(model)
+    torch.cuda.synchronize()
+    comp, tok_c, sums_c, full_c = generate_timed(model, ids, n, keep=2, warm_tokens=n)
+    same = (bool(torch.equal(tok_u, tok_c)) and bool(torch.equal(sums_u, sums_c))
+            and all(torch.equal(a, b) for a, b in zip(full_u, full_c)))
+    out = {
+        "workload": f"config 3 (bounded): Qwen3-8B architecture, 36 layers, batch 16 x 128 prompt ids, {n} greedy "
+                    "new tokens, HF generate with the dynamic cache",
+        "fp8_matmul": fp8_model.fp8_matmul_backend(),
+        "uncompressed_tokens_per_s": round(unc["tokens_per_s"], 2),
+        "compressed_tokens_per_s": round(comp["tokens_per_s"], 2),
+        "compressed_vs_uncompressed": round(comp["tokens_per_s"] / unc["tokens_per_s"], 4),
+        "uncompressed_ms_per_step": round(unc["ms_per_step"], 3),
+        "compressed_ms_per_step": round(comp["ms_per_step"], 3),
+        "peak_hbm_mb": {"uncompressed": round(unc["peak_hbm_mb"]), "compressed": round(comp["peak_hbm_mb"])},
+        "identical_tokens_and_logits": same,
+        "build_and_run_s": round(time.time() - t0, 1),
+    }
+    del model
+    TensorManager.clear_device()
+    return out
+
+
 def run_ours(args, rank, world, dev):
     from ecf8_b200 import _lib
-    from ecf8_b200.run import HostStreamDecoder, TensorManager, decode_streams
+    from ecf8_b200.run import TensorManager, decode_streams
     L = _lib.lib()
     stream = torch.cuda.current_stream(dev)
-    if world == 1:
+    workload = pick_workload(args)
+    if workload == "config2":
+        if world > 1:
+            raise SystemExit("config 2 is a one-GPU workload; run it without torchrun")
         layers, originals = build_qwen3_8b(dev, args.layers)
         n_max = max(c["packed_other_4bits"].numel() * 2 for c in layers)
         scratch = TensorManager.get_tensor(dev, n_max).view(torch.uint8)
@@ -256,6 +391,7 @@ def run_ours(args, rank, world, dev):
         elems = sum(c["packed_other_4bits"].numel() * 2 for c in layers)
         algo = sum(stream_bytes(c) for c in layers)
         launches_per_step = len(calls)
+        n_launch_groups = len(calls)
 
         def step():
             for a in calls:
@@ -273,51 +409,48 @@ def run_ours(args, rank, world, dev):
             off += (n + 15) & ~15
         elems = sum(sum(s["packed_other_4bits"].numel() * 2 for s in ly) for ly in layers)
         algo = sum(sum(stream_bytes(s) for s in ly) for ly in layers)
-        launches_per_step = len(layers) * math.ceil(len(layers[0]) / 128)
+        launches_per_step = len(layers) * math.ceil(len(layers[0]) / _lib.MAX_BATCH)
+        n_launch_groups = launches_per_step
 
         def step():
             for ly in layers:
                 decode_streams(ly, outs, stream=stream, overlap_previous=True)
 
-    # warm-up, then the timed region: K steps between a barrier + sync on both sides
+    # warm-up, then the timed region: exactly K steps between a barrier + sync on both sides
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    n_launch_groups = len(calls) if world == 1 else len(layers)
-    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(world)
-    torch.cuda.synchronize()
-    with ClockSampler(dev.index) as clk:
-        t_start.record(stream)
-        for k in range(args.steps):
-            step()
-        t_end.record(stream)
-        torch.cuda.synchronize()
-    barrier(world)
-    ms_total = t_start.elapsed_time(t_end)
-    ms_step = max_over_ranks(ms_total / args.steps, world)
+    ms_step, ms_total, clocks = timed_steps(step, args.steps, stream, world, dev)
     # The timed region holds nothing but the decode launches, back to back
     # (each may overlap its set-up with the previous one's end), so the mean
     # launch duration is this rank's device time over its launches; no events
     # between launches, which would order them fully.
     mean_launch_ms = ms_total / (args.steps * n_launch_groups)
 
+    # Steady state: at least --steady-s seconds of device time (same steps),
+    # so that the clock samples see the kernel at its sustained clocks.
+    steady = None
+    if args.steady_s > 0:
+        k2 = max(args.steps, math.ceil(args.steady_s * 1e3 / ms_step))
+        ms2, total2, clk2 = timed_steps(step, k2, stream, world, dev)
+        steady = {"steps": k2, "ms_per_step": round(ms2, 4), "device_s": round(total2 / 1e3, 3),
+                  "mean_launch_us": round(total2 / (k2 * n_launch_groups) * 1e3, 2), "clocks": clk2}
+
     # bit-exactness after timing
     exact = True
-    if world == 1:
+    if workload == "config2":
         for c, orig in zip(layers, originals):
             n = c["packed_other_4bits"].numel() * 2
             L.ecf8_decode_batch_flags(*decode_args(L, c, scratch, stream))
             exact &= bool(torch.equal(scratch[:n], orig))
     else:
+        _, plan = moe_plan(rank, world, args.moe_layers)
         rng = np.random.default_rng(rank)
         for l in rng.choice(len(layers), size=min(3, len(layers)), replace=False):
             decode_streams(layers[l], outs, stream=stream)
-            want = make_stream_weights(QWEN3_235B_ATTN, (int(l) * 1000 + 999) * 10, dev).view(torch.uint8)
-            exact &= bool(torch.equal(outs[0], want))
-            e = owned[len(owned) // 2]
-            want = make_stream_weights(QWEN3_235B_EXPERT, (int(l) * 1000 + e) * 10, dev).view(torch.uint8)
-            exact &= bool(torch.equal(outs[1 + len(owned) // 2], want))
+            for j in (0, 1, len(owned) // 2, len(owned)):
+                _, seed, shapes = plan[l][j]
+                exact &= bool(torch.equal(outs[j], make_stream_weights(shapes, seed, dev).view(torch.uint8)))
     torch.cuda.synchronize()
     exact = max_over_ranks(0.0 if exact else 1.0, world) == 0.0
 
@@ -327,42 +460,63 @@ def run_ours(args, rank, world, dev):
     # roofline of the dominant kernel: per-launch algorithmic bytes / mean launch time
     per_launch_bytes = algo / n_launch_groups
     achieved = per_launch_bytes / (mean_launch_ms * 1e-3) / 1e9
-    traffic = profiled_traffic("decode_kernel_qwen3_8b_layer.md" if world == 1 else "none")
+    traffic = profiled_traffic("decode_kernel_qwen3_8b_layer.md" if workload == "config2"
+                               else "decode_kernel_config5_layer.md")
+    if steady is not None:
+        steady["roofline_frac"] = round(per_launch_bytes / (steady["mean_launch_us"] * 1e-6) / 1e9 / peak, 4)
+        steady["value"] = round(total_elems / (steady["ms_per_step"] * 1e-3) / 1e9, 2)
 
     # end to end through the host-buffer API: pinned host in, decode, pinned host out
     e2e = None
     if not args.no_e2e:
-        if world == 1:
+        if workload == "config2":
             e2e = run_e2e(args, layers, originals[-1], dev, world)
         else:  # a bounded sample of this rank's shard: its first two layers' streams
+            _, plan = moe_plan(rank, world, args.moe_layers)
             sample = [s for ly in layers[:2] for s in ly]
             l_last = min(2, len(layers)) - 1
-            want = make_stream_weights(QWEN3_235B_EXPERT, (l_last * 1000 + owned[-1]) * 10, dev).view(torch.uint8)
-            e2e = run_e2e(args, sample, want, dev, world)
+            _, seed, shapes = plan[l_last][-1]
+            e2e = run_e2e(args, sample, make_stream_weights(shapes, seed, dev).view(torch.uint8), dev, world)
             e2e["sample"] = f"first {l_last + 1} layers of each rank's shard (attention + {len(owned)} experts each)"
 
-    cpu = cpu_baseline(layers[0]) if (world == 1 and rank == 0 and not args.no_cpu_baseline) else None
+    conv = None
+    if workload == "config2" and not args.no_call_conventions:
+        conv = call_convention_times(L, layers[0], scratch, stream)
+    gen = None
+    if workload == "config2" and args.gen_tokens > 0:
+        del calls, scratch
+        torch.cuda.empty_cache()
+        gen = run_generation(args, dev)
+    cpu = cpu_baseline(layers[0]) if (workload == "config2" and rank == 0 and not args.no_cpu_baseline) else None
     if rank != 0:
         return None
-    cfg = {
-        "workload": (f"config 2: Qwen3-8B-shaped FP8 weight set decode, {len(layers)} layer streams x 192,937,984 "
-                     "e4m3 weights, one launch per layer into the shared scratch" if world == 1 else
-                     f"config 5: Qwen3-235B-A22B-shaped MoE decode, {args.moe_layers} layers, 128 experts "
-                     f"x 18,874,368 weights split {QWEN3_235B_EXPERTS // world}/GPU + attention replica "
-                     "(71,303,168) per GPU, one batched launch per layer"),
+    if workload == "config2":
+        cfg = {
+            "workload": (f"config 2: Qwen3-8B-shaped FP8 weight set decode, {len(layers)} layer streams x "
+                         "192,937,984 e4m3 weights, one launch per layer into the shared scratch"),
+            "parallelism": "single GPU",
+            "compressed_bits_per_element": sum(
+                (c["encoded"].numel() + c["packed_other_4bits"].numel()) * 8 for c in layers) / elems,
+        }
+    else:
+        cfg = {
+            "workload": (f"config 5: Qwen3-235B-A22B-shaped MoE decode, {args.moe_layers} layers, 128 experts "
+                         f"x 18,874,368 weights split {QWEN3_235B_EXPERTS // world}/GPU + attention replica "
+                         "(71,303,168) per GPU, one batched launch per layer (up to 128 streams per launch)"),
+            "parallelism": f"expert-sharded x{world}, no data-path collective",
+            "scaling_note": ("all 128 experts of every layer are split over the ranks (fixed total); each rank "
+                             "also decodes a replica of the attention stream, counted in value"),
+        }
+    cfg.update({
         "elements_per_step": int(total_elems),
         "algorithmic_bytes_per_step_per_gpu": int(algo),
         "bytes_per_element": algo / elems,
         "l2": "inputs larger than L2 (no flush needed): "
               f"{algo / 2 ** 30:.2f} GiB touched per step per GPU vs 126 MiB L2",
         "weights": "N(0,0.02), 128x128 block scales absmax->448, e4m3fn; seeded per Linear",
-        "decode_tables": "prepared once per stream at load (ecf8_build_table), 80 KB each",
-        "parallelism": f"expert-sharded x{world}, no data-path collective" if world > 1 else "single GPU",
+        "decode_tables": f"prepared once per stream at load (ecf8_build_table), {_lib.TABLE_BYTES} B each",
         "bit_exact": exact,
-    }
-    if world == 1:
-        cfg["compressed_bits_per_element"] = sum(
-            (c["encoded"].numel() + c["packed_other_4bits"].numel()) * 8 for c in layers) / elems
+    })
     line = {
         "metric": "ECF8 decode GB/s (fp8 out)",
         "value": round(value, 2),
@@ -372,7 +526,7 @@ def run_ours(args, rank, world, dev):
         "warmup": args.warmup,
         "ms_per_step": round(ms_step, 4),
         "higher_is_better": True,
-        "scaling": "weak" if world == 1 else "strong",
+        "scaling": "weak" if workload == "config2" else "strong",
         "vs_baseline": None,
         "dtype": "u8",
         "data": "synthetic (seeded random-init weights of the named shapes)",
@@ -390,11 +544,16 @@ def run_ours(args, rank, world, dev):
             "algorithmic_bytes_per_launch": int(per_launch_bytes),
             "mean_launch_us": round(mean_launch_ms * 1e3, 2),
         },
+        "steady_state": steady,
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": launches_per_step * args.steps,
-        "clocks": clk.summary(),
+        "clocks": clocks,
     }
+    if conv is not None:
+        line["call_conventions"] = conv
+    if gen is not None:
+        line["generation"] = gen
     return line
 
 
@@ -469,73 +628,103 @@ def cpu_baseline(c, budget_s=10.0):
 # Reference arm
 # ---------------------------------------------------------------------------
 
+def reference_sample_streams(oracle, workload):
+    """The reference arm's sample of the bench workload, as host streams built
+    with the restated reference codec: config 2 -> layer 0 (one stream);
+    config 5 -> layer 0's attention stream and its first four experts."""
+    from dahuffman import HuffmanCodec
+    if workload == "config2":
+        groups = [(QWEN3_8B_LINEARS, 0)]
+    else:
+        _, plan = moe_plan(0, 1, 1)
+        groups = [(shapes, seed) for _, seed, shapes in plan[0][:5]]
+    out = []
+    for shapes, seed0 in groups:
+        parts = []
+        for k, (_, o, i) in enumerate(shapes):
+            g = torch.Generator().manual_seed(seed0 + k)
+            parts.append(quantize_block128(torch.randn(o, i, generator=g) * 0.02).reshape(-1))
+        fp8 = torch.cat(parts).view(torch.uint8).numpy()
+        e, packed = oracle.split(fp8)
+        cnt = np.bincount(e, minlength=16)
+        codec = HuffmanCodec.from_frequencies({s: int(c) for s, c in enumerate(cnt) if c})
+        table = codec.get_code_table()
+        bits = np.zeros(16, np.uint8)
+        vals = np.zeros(16, np.uint32)
+        for s, (b, v) in table.items():
+            if isinstance(s, int):
+                bits[s], vals[s] = b, v
+        eb, ev = table[codec._eof]
+        luts = oracle.luts_from_table(table)
+        enc, gaps, op = oracle.encode(e, bits, vals, eb, ev)
+        out.append(({"luts": luts, "encoded": enc, "packed": packed, "gaps": gaps, "output_positions": op}, fp8))
+    return out
+
+
 def run_reference(args):
     """The reference decode on the host cores: the oracle's C restatement of
-    dfloat/run/decode.cu (the reference has no CPU decoder), on layer 0 of the
-    config-2 weight set, code table from the reference's Huffman dependency
-    (restated) and LUTs / stream from restatements of its codec."""
+    dfloat/run/decode.cu (the reference has no CPU decoder), on a sample of the
+    bench's own workload (config 2, or config 5 under torchrun), code tables
+    from the reference's Huffman dependency (restated) and LUTs / streams from
+    restatements of its codec.  A step decodes every sample stream once."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle
-    from dahuffman import HuffmanCodec
+    workload = pick_workload(args)
     t0 = time.time()
-    parts = []
-    for k, (_, o, i) in enumerate(QWEN3_8B_LINEARS):
-        g = torch.Generator().manual_seed(k)
-        parts.append(quantize_block128(torch.randn(o, i, generator=g) * 0.02).reshape(-1))
-    fp8 = torch.cat(parts).view(torch.uint8).numpy()
-    e, packed = oracle.split(fp8)
-    cnt = np.bincount(e, minlength=16)
-    codec = HuffmanCodec.from_frequencies({s: int(c) for s, c in enumerate(cnt) if c})
-    table = codec.get_code_table()
-    bits = np.zeros(16, np.uint8)
-    vals = np.zeros(16, np.uint32)
-    for s, (b, v) in table.items():
-        if isinstance(s, int):
-            bits[s], vals[s] = b, v
-    eb, ev = table[codec._eof]
-    luts = oracle.luts_from_table(table)
-    enc, gaps, op = oracle.encode(e, bits, vals, eb, ev)
-    s = {"luts": luts, "encoded": enc, "packed": packed, "gaps": gaps, "output_positions": op}
-    log(f"reference arm: built layer-0 sample in {time.time() - t0:.1f}s")
-    n = fp8.size
-    out = np.empty(n, np.uint8)
+    sample = reference_sample_streams(oracle, workload)
+    log(f"reference arm: built the {workload} sample in {time.time() - t0:.1f}s")
+    outs = [np.empty(fp8.size, np.uint8) for _, fp8 in sample]
     t1 = time.perf_counter()
-    oracle.decode(s, out=out)
+    for (s, fp8), out in zip(sample, outs):
+        oracle.decode(s, out=out)
+        assert np.array_equal(out, fp8), "oracle decode is not bit-exact"
     first = time.perf_counter() - t1
-    assert np.array_equal(out, fp8), "oracle decode is not bit-exact"
-    # keep the whole run within a few minutes: shrink the sample to a prefix of groups
+    # keep the whole run within a few minutes: shrink each stream to a prefix of groups
     budget = 150.0 / max(1, args.steps + args.warmup)
     if first > budget:
-        groups = max(1, int((op.size - 1) * budget / first))
-        end = int(op[groups])
-        s = {"luts": luts, "encoded": enc[:groups * 4096], "packed": packed[:end // 2],
-             "gaps": gaps[:groups * 256], "output_positions": np.concatenate([op[:groups], [end]]).astype(np.uint64)}
-        n = end
-        out = np.empty(n, np.uint8)
+        frac = budget / first
+        cut = []
+        for s, fp8 in sample:
+            op = s["output_positions"]
+            groups = max(1, int((op.size - 1) * frac))
+            end = int(op[groups])
+            cut.append(({"luts": s["luts"], "encoded": s["encoded"][:groups * 4096], "packed": s["packed"][:end // 2],
+                         "gaps": s["gaps"][:groups * 256],
+                         "output_positions": np.concatenate([op[:groups], [end]]).astype(np.uint64)}, fp8[:end]))
+        sample = cut
+        outs = [np.empty(fp8.size, np.uint8) for _, fp8 in sample]
+    n = sum(fp8.size for _, fp8 in sample)
+
+    def step():
+        for (s, _), out in zip(sample, outs):
+            oracle.decode(s, out=out)
     for _ in range(args.warmup):
-        oracle.decode(s, out=out)
+        step()
     times = []
     for _ in range(args.steps):
         t1 = time.perf_counter()
-        oracle.decode(s, out=out)
+        step()
         times.append(time.perf_counter() - t1)
     dt = statistics.mean(times)
     value = n / dt / 1e9
     cores = oracle.max_threads()
+    what = ("config 2 sample: layer 0 of the Qwen3-8B-shaped weight set" if workload == "config2" else
+            "config 5 sample: layer 0 attention stream + experts 0-3 of the Qwen3-235B-A22B-shaped set")
     line = {
         "metric": "ECF8 decode GB/s (fp8 out)", "value": round(value, 3), "unit": "GB/s", "n_gpus": 1,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
         "data": "synthetic (seeded random-init weights of the named shapes)",
-        "config": {"workload": "config 2 sample: layer 0 of the Qwen3-8B-shaped weight set"
-                               f" ({n:,} e4m3 weights per step)"},
+        "config": {"workload": f"{what} ({n:,} e4m3 weights per step)"},
         "impl": "reference",
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": f"{n:,} weights per step, C restatement of dfloat/run/decode.cu "
                                    "(the reference ships no CPU decoder), OpenMP over groups"},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "reference_gpu_kernel": reference_gpu_kernel(oracle, s, n, fp8[:n], args),
     }
+    if workload == "config2":
+        s, fp8 = sample[0]
+        line["reference_gpu_kernel"] = reference_gpu_kernel(oracle, s, fp8.size, fp8, args)
     return line
 
 
@@ -594,8 +783,15 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ecf8", "reference"], default="ecf8")
-    ap.add_argument("--moe-layers", type=int, default=QWEN3_235B_LAYERS)
-    ap.add_argument("--e2e-steps", type=int, default=3)
+    ap.add_argument("--moe-layers", type=int, default=MOE_BENCH_LAYERS)
+    ap.add_argument("--workload", choices=["auto", "config2", "config5"], default="auto",
+                    help="auto: config 5 under torchrun (any world size), config 2 otherwise")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--steady-s", type=float, default=1.0,
+                    help="device seconds of the steady-state measurement after the K timed steps (0: off)")
+    ap.add_argument("--no-call-conventions", action="store_true")
+    ap.add_argument("--gen-tokens", type=int, default=64,
+                    help="config-3 generation measured after the decode bench (new tokens per arm; 0: off)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--layers", type=int, default=QWEN3_8B_LAYERS,
@@ -610,7 +806,7 @@ def main():
         return
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
+    if under_torchrun():
         import datetime
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
@@ -619,7 +815,7 @@ def main():
     try:
         line = run_ours(args, rank, world, dev)
     finally:
-        if world > 1:
+        if under_torchrun():
             import torch.distributed as dist
             dist.barrier()
             dist.destroy_process_group()

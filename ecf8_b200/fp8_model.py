@@ -8,8 +8,14 @@ this environment has, so this module builds the same model shape itself:
 
 * `Fp8Linear`: weight e4m3 [out, in] + `weight_scale_inv` f32 [ceil(out/128),
   ceil(in/128)], the layout of FP8 checkpoints such as Qwen3-8B-FP8.  Its
-  forward expands the block scales and runs a bf16 matmul; compressed and
-  uncompressed models share it, so decoded weights give identical logits.
+  forward is a block-scaled FP8 GEMM that reads the e4m3 weight directly
+  (activations quantized per 1x128 group, weights scaled per 128x128 tile,
+  the scheme of transformers' FP8Linear), through the CUTLASS kernel of the
+  installed vLLM; where that is unavailable (no vLLM, a CPU tensor, shapes
+  that are not multiples of 128) it expands the block scales and runs a bf16
+  matmul.  `set_fp8_matmul("dequant")` forces the second path.  Compressed
+  and uncompressed models share the layer, so decoded weights give identical
+  logits.
 * `fp8_model_from_config`: a transformers model from its config with every
   Linear of the decoder layers replaced by an `Fp8Linear` (random weights
   N(0, std) quantized per 128x128 tile, absmax -> 448, seeded per layer), or
@@ -28,6 +34,39 @@ import torch.nn.functional as F
 
 E4M3_MAX = 448.0
 BLOCK = 128
+
+_MATMUL = {"mode": "auto", "ops": None, "quant": None, "failed": None}
+
+
+def set_fp8_matmul(mode):
+    """"auto" (block-scaled FP8 GEMM where available) or "dequant" (e4m3 ->
+    bf16 expansion by the block scales, then a bf16 matmul)."""
+    if mode not in ("auto", "dequant"):
+        raise ValueError(mode)
+    _MATMUL["mode"] = mode
+
+
+def fp8_matmul_backend():
+    """The FP8 GEMM that Fp8Linear uses on CUDA tensors: "cutlass-blockwise"
+    or "dequant-bf16"."""
+    return "cutlass-blockwise" if _cutlass_ops() is not None else "dequant-bf16"
+
+
+def _cutlass_ops():
+    if _MATMUL["mode"] != "auto" or _MATMUL["failed"]:
+        return None
+    if _MATMUL["ops"] is None:
+        try:
+            import vllm._custom_ops as ops
+            from vllm.model_executor.layers.quantization.utils.fp8_utils import per_token_group_quant_fp8
+            if not torch.cuda.is_available() or not ops.cutlass_scaled_mm_supports_block_fp8(
+                    torch.cuda.get_device_capability()[0] * 10 + torch.cuda.get_device_capability()[1]):
+                raise RuntimeError("no block-scaled FP8 GEMM for this device")
+            _MATMUL["ops"], _MATMUL["quant"] = ops, per_token_group_quant_fp8
+        except Exception as e:  # the bf16 expansion path serves both arms alike
+            _MATMUL["failed"] = repr(e)
+            return None
+    return _MATMUL["ops"]
 
 
 class Fp8Linear(nn.Module):
@@ -49,7 +88,19 @@ class Fp8Linear(nn.Module):
         return (self.weight.float() * s).to(dtype)
 
     def forward(self, x):
-        return F.linear(x, self.dequantized(x.dtype), self.bias)
+        o, i = self.out_features, self.in_features
+        ops = _cutlass_ops() if x.is_cuda and o % BLOCK == 0 and i % BLOCK == 0 else None
+        if ops is None:
+            return F.linear(x, self.dequantized(x.dtype), self.bias)
+        x2 = x.reshape(-1, i)
+        if not x2.is_contiguous():
+            x2 = x2.contiguous()
+        xq, xs = _MATMUL["quant"](x2, BLOCK, column_major_scales=True, use_ue8m0=False)
+        y = ops.cutlass_scaled_mm(xq, self.weight.t(), scale_a=xs, scale_b=self.weight_scale_inv.t(),
+                                  out_dtype=x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16)
+        if self.bias is not None:
+            y = y + self.bias.to(y.dtype)
+        return y.reshape(*x.shape[:-1], o).to(x.dtype)
 
     def extra_repr(self):
         return f"in_features={self.in_features}, out_features={self.out_features}, e4m3 128x128"

@@ -19,7 +19,9 @@ the arms are comparable; each arm first runs one untimed generation of the
 same length, so that neither pays the allocator's first-growth cost.  Every step's logits are checked: the first steps in
 full, all steps by a per-row float64 sum, plus the generated tokens.
 
-Both arms use the same FP8 Linear (ecf8_b200.fp8_model.Fp8Linear), so
+Both arms use the same FP8 Linear (ecf8_b200.fp8_model.Fp8Linear: a
+block-scaled FP8 GEMM reading e4m3 weights directly, or with
+--fp8_matmul dequant the e4m3 -> bf16 expansion and a bf16 matmul), so
 identical decoded weights must give identical logits.
 """
 
@@ -125,9 +127,12 @@ def main(argv=None):
     ap.add_argument("--compressed_only", action="store_true", help="compressed arm only")
     ap.add_argument("--keep", type=int, default=4, help="steps whose full logits are compared")
     ap.add_argument("--warm_tokens", type=int, default=None, help="warm-up generation length (default: num_tokens)")
+    ap.add_argument("--fp8_matmul", choices=["auto", "dequant"], default="auto",
+                    help="auto: block-scaled FP8 GEMM on e4m3 weights; dequant: bf16 expansion + bf16 matmul")
     args = ap.parse_args(argv)
     from .compress import compress_model_in_place
-    from .fp8_model import fp8_model_from_config, load_fp8_checkpoint
+    from .fp8_model import fp8_matmul_backend, fp8_model_from_config, load_fp8_checkpoint, set_fp8_matmul
+    set_fp8_matmul(args.fp8_matmul)
     from .run import TensorManager
     dev = torch.device("cuda", torch.cuda.current_device())
     t0 = time.time()
@@ -143,7 +148,8 @@ def main(argv=None):
     ids = torch.randint(0, model.config.vocab_size, (args.batch_size, args.prompt_len), generator=g, device=dev)
     fp8_bytes, _ = _model_bytes(model)
     line = {"workload": workload, "batch_size": args.batch_size, "prompt_len": args.prompt_len,
-            "new_tokens": args.num_tokens, "decoding": "greedy", "model_build_s": round(build_s, 1)}
+            "new_tokens": args.num_tokens, "decoding": "greedy", "model_build_s": round(build_s, 1),
+            "fp8_matmul": fp8_matmul_backend()}
     ref = None
     if not args.compressed_only:
         res, tokens, sums, full = generate_timed(model, ids, args.num_tokens, args.keep, args.warm_tokens)
