@@ -45,7 +45,7 @@ from .codec import (
     locate_block_by_regex,
 )
 from .const import get_fp8_pattern_dict
-from .fp8_model import Fp8Linear, load_fp8_checkpoint
+from .fp8_model import Fp8FusedExperts, Fp8Linear, fused_experts_owner, load_fp8_checkpoint
 from .run import decode_stream, get_dfloat_model_name_or_path
 
 package_version = "0.2.0"
@@ -156,12 +156,20 @@ def process_all_fp8_blocks_parallel(fp8_layers_by_block, num_processes=1, revers
 def find_fp8_blocks(model, model_fp8_regex):
     """{block name: {layer name: module}} for a family's FP8 pattern: a list of
     block regexes (every e4m3 Linear inside), or {regex: [layer paths]}
-    (compress.py:506-537)."""
+    (compress.py:506-537).  Experts held in a fused block (Fp8FusedExperts,
+    transformers' 3-D expert parameters) count as the per-expert blocks
+    "<experts>.M" of the reference layout, with views as their sub-Linears."""
     blocks = {}
     if isinstance(model_fp8_regex, list):
-        for block_name, block in locate_block_by_regex(model, "|".join(model_fp8_regex)).items():
+        joined = "|".join(model_fp8_regex)
+        for block_name, block in locate_block_by_regex(model, joined).items():
             blocks[block_name] = find_layers_by_data_type_and_layer_type(
                 block, target_dtype=torch.float8_e4m3fn, layers=_fp8_layer_types(), name=block_name)
+        for name, mod in model.named_modules():
+            if isinstance(mod, Fp8FusedExperts) and mod._has_dense():
+                for m in range(mod.num_experts):
+                    if re.fullmatch(joined, f"{name}.{m}"):
+                        blocks[f"{name}.{m}"] = mod.expert_layers(m, f"{name}.{m}")
     else:
         for regex, selected in model_fp8_regex.items():
             for block_name, block in locate_block_by_regex(model, regex).items():
@@ -206,14 +214,20 @@ def compress_model(model, save_path, threads_per_block=512, bytes_per_thread=8, 
     entropy_rows = {}
     for result in results:
         block_name = result["block_name"]
-        sub_module = operator.attrgetter(block_name)(model)
         entropy_rows[block_name] = result["entropy"]
         tensors = load_file(result["block_save_path"])
         if validate_cuda:
             validate_cuda_decoding_fp8(result, tensors, device)
-        _delete_layer_weights(model, block_name, sub_module, result["layers_to_delete"])
-        for key in STREAM_KEYS:
-            sub_module.register_buffer(key, tensors[key])
+        fused = fused_experts_owner(model, block_name + ".encoded")
+        if fused is not None:  # one expert of a fused block: the block drops its dense weights itself
+            owner, m, _ = fused
+            for key in STREAM_KEYS:
+                owner.add_expert_stream(m, key, tensors[key], threads_per_block, bytes_per_thread)
+        else:
+            sub_module = operator.attrgetter(block_name)(model)
+            _delete_layer_weights(model, block_name, sub_module, result["layers_to_delete"])
+            for key in STREAM_KEYS:
+                sub_module.register_buffer(key, tensors[key])
         matched = result["matched_regex"]
         if matched:
             if fp8_regex_dict[matched] is None:
@@ -306,6 +320,12 @@ def compress_model_in_place(model, threads_per_block=512, bytes_per_thread=8, de
         tensors = {"luts": c["luts"], "encoded": c["encoded"], "packed_other_4bits": c["packed_other_4bits"],
                    "output_positions": c["output_positions"].view(torch.uint8), "gaps": c["gaps"],
                    "split_positions": split_positions}
+        fused = fused_experts_owner(model, block_name + ".encoded")
+        if fused is not None:
+            owner, m, _ = fused
+            for key in ("luts", "packed_other_4bits", "output_positions", "gaps", "split_positions", "encoded"):
+                owner.add_expert_stream(m, key, tensors[key], threads_per_block, bytes_per_thread)
+            continue
         module = operator.attrgetter(block_name)(model)
         for key in ("luts", "packed_other_4bits", "output_positions", "gaps", "split_positions", "encoded"):
             _process_compressed_tensor(module, key, tensors[key], f"{block_name}.{key}", {regex: names},

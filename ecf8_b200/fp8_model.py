@@ -16,10 +16,18 @@ this environment has, so this module builds the same model shape itself:
   matmul.  `set_fp8_matmul("dequant")` forces the second path.  Compressed
   and uncompressed models share the layer, so decoded weights give identical
   logits.
+* `Fp8FusedExperts`: the FP8 form of transformers' fused MoE experts
+  (`Qwen3MoeExperts`, whose experts are 3-D `gate_up_proj` / `down_proj`
+  parameters), e4m3 with 128x128 block scales per expert.  Its state dict
+  uses the per-expert keys of FP8 checkpoints and of the reference's
+  compressed layout (`...mlp.experts.M.{gate,up,down}_proj.weight[_scale_inv]`,
+  and `...mlp.experts.M.{luts,encoded,...}` once compressed: one ECF8 stream
+  per expert, dfloat/const.py:15-21).  Compressed, its forward decodes only
+  the experts the router picked, in one batched launch.
 * `fp8_model_from_config`: a transformers model from its config with every
-  Linear of the decoder layers replaced by an `Fp8Linear` (random weights
-  N(0, std) quantized per 128x128 tile, absmax -> 448, seeded per layer), or
-  uninitialised for loading.
+  Linear of the decoder layers replaced by an `Fp8Linear` and every fused
+  expert block by an `Fp8FusedExperts` (random weights N(0, std) quantized per
+  128x128 tile, absmax -> 448, seeded per layer), or uninitialised for loading.
 * `load_fp8_checkpoint`: the same from a local FP8 checkpoint directory
   (config.json + *.safetensors), read directly.
 """
@@ -69,6 +77,35 @@ def _cutlass_ops():
     return _MATMUL["ops"]
 
 
+def dequantize_block128(weight, scale_inv, dtype=torch.bfloat16):
+    """e4m3 [out, in] times its 128x128 tile scales, in `dtype`."""
+    o, i = weight.shape
+    if o % BLOCK == 0 and i % BLOCK == 0:  # one broadcast multiply per 128x128 tile
+        w = weight.reshape(o // BLOCK, BLOCK, i // BLOCK, BLOCK).to(dtype)
+        return (w * scale_inv.to(dtype)[:, None, :, None]).reshape(o, i)
+    s = scale_inv.repeat_interleave(BLOCK, 0)[:o].repeat_interleave(BLOCK, 1)[:, :i]
+    return (weight.float() * s).to(dtype)
+
+
+def fp8_linear(x, weight, scale_inv, bias=None):
+    """x @ (weight * tile scales)^T for an e4m3 weight [out, in] with 128x128
+    block scales: the block-scaled FP8 GEMM (activations quantized per 1x128
+    group) where available, else the bf16 expansion."""
+    o, i = weight.shape
+    ops = _cutlass_ops() if x.is_cuda and o % BLOCK == 0 and i % BLOCK == 0 else None
+    if ops is None:
+        return F.linear(x, dequantize_block128(weight, scale_inv, x.dtype), bias)
+    x2 = x.reshape(-1, i)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    xq, xs = _MATMUL["quant"](x2, BLOCK, column_major_scales=True, use_ue8m0=False)
+    y = ops.cutlass_scaled_mm(xq, weight.t(), scale_a=xs, scale_b=scale_inv.t(),
+                              out_dtype=x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16)
+    if bias is not None:
+        y = y + bias.to(y.dtype)
+    return y.reshape(*x.shape[:-1], o).to(x.dtype)
+
+
 class Fp8Linear(nn.Module):
     def __init__(self, in_features, out_features, bias=False, device=None):
         super().__init__()
@@ -80,30 +117,225 @@ class Fp8Linear(nn.Module):
         self.bias = nn.Parameter(torch.zeros(out_features, device=device), requires_grad=False) if bias else None
 
     def dequantized(self, dtype=torch.bfloat16):
-        o, i = self.out_features, self.in_features
-        if o % BLOCK == 0 and i % BLOCK == 0:  # one broadcast multiply per 128x128 tile
-            w = self.weight.view(o // BLOCK, BLOCK, i // BLOCK, BLOCK).to(dtype)
-            return (w * self.weight_scale_inv.to(dtype)[:, None, :, None]).view(o, i)
-        s = self.weight_scale_inv.repeat_interleave(BLOCK, 0)[:o].repeat_interleave(BLOCK, 1)[:, :i]
-        return (self.weight.float() * s).to(dtype)
+        return dequantize_block128(self.weight, self.weight_scale_inv, dtype)
 
     def forward(self, x):
-        o, i = self.out_features, self.in_features
-        ops = _cutlass_ops() if x.is_cuda and o % BLOCK == 0 and i % BLOCK == 0 else None
-        if ops is None:
-            return F.linear(x, self.dequantized(x.dtype), self.bias)
-        x2 = x.reshape(-1, i)
-        if not x2.is_contiguous():
-            x2 = x2.contiguous()
-        xq, xs = _MATMUL["quant"](x2, BLOCK, column_major_scales=True, use_ue8m0=False)
-        y = ops.cutlass_scaled_mm(xq, self.weight.t(), scale_a=xs, scale_b=self.weight_scale_inv.t(),
-                                  out_dtype=x.dtype if x.dtype in (torch.bfloat16, torch.float16) else torch.bfloat16)
-        if self.bias is not None:
-            y = y + self.bias.to(y.dtype)
-        return y.reshape(*x.shape[:-1], o).to(x.dtype)
+        return fp8_linear(x, self.weight, self.weight_scale_inv, self.bias)
 
     def extra_repr(self):
         return f"in_features={self.in_features}, out_features={self.out_features}, e4m3 128x128"
+
+
+_STREAM_KEYS = ("luts", "encoded", "packed_other_4bits", "output_positions", "gaps", "split_positions")
+_DENSE_KEYS = ("gate_proj.weight", "up_proj.weight", "down_proj.weight", "gate_proj.weight_scale_inv",
+               "up_proj.weight_scale_inv", "down_proj.weight_scale_inv")
+
+
+class _ExpertLinearView:
+    """One expert's sub-Linear inside a fused parameter, as the compressor's
+    block walk sees a Linear: a `weight` (a view) and its shape."""
+
+    def __init__(self, weight):
+        self.weight = weight
+        self.out_features, self.in_features = weight.shape
+
+
+class Fp8FusedExperts(nn.Module):
+    """transformers' fused MoE experts (Qwen3MoeExperts: `gate_up_proj`
+    [E, 2I, H], `down_proj` [E, H, I], gate rows before up rows) in e4m3 with
+    128x128 block scales per expert.  Same forward contract and the same
+    routing loop as transformers' eager implementation; each expert's matmuls
+    go through `fp8_linear`.
+
+    Compressed (`add_expert_stream`), expert M is one ECF8 stream: its
+    down, gate and up weights concatenated in that (sorted-name) order, which
+    is down_proj[M] followed by gate_up_proj[M].  The dense parameters are
+    dropped once every expert has its stream; the forward then decodes the
+    experts the router picked, in one batched launch, into the per-device
+    scratch (the same TensorManager buffer the block hooks use: the block's
+    attention has run by then) and uses views of it."""
+
+    def __init__(self, num_experts, hidden_size, intermediate_size, act_fn, device=None):
+        super().__init__()
+        if hidden_size % BLOCK or intermediate_size % BLOCK:
+            raise ValueError("expert sizes must be multiples of 128 for 128x128 block scales")
+        self.num_experts, self.hidden_dim, self.intermediate_dim = num_experts, hidden_size, intermediate_size
+        e, h, i = num_experts, hidden_size, intermediate_size
+        self.gate_up_proj = nn.Parameter(torch.empty(e, 2 * i, h, dtype=torch.float8_e4m3fn, device=device),
+                                         requires_grad=False)
+        self.down_proj = nn.Parameter(torch.empty(e, h, i, dtype=torch.float8_e4m3fn, device=device),
+                                      requires_grad=False)
+        self.register_buffer("gate_up_proj_scale_inv",
+                             torch.ones(e, 2 * i // BLOCK, h // BLOCK, dtype=torch.float32, device=device))
+        self.register_buffer("down_proj_scale_inv",
+                             torch.ones(e, h // BLOCK, i // BLOCK, dtype=torch.float32, device=device))
+        self.act_fn = act_fn
+        self.compressed = set()
+        self.threads_per_block, self.bytes_per_thread = 512, 8
+
+    # -- per-expert views -----------------------------------------------------
+    def expert_layers(self, m, prefix):
+        """{sub-Linear name: view} of expert m's dense weights, in sorted order."""
+        i = self.intermediate_dim
+        return {f"{prefix}.down_proj": _ExpertLinearView(self.down_proj.data[m]),
+                f"{prefix}.gate_proj": _ExpertLinearView(self.gate_up_proj.data[m, :i]),
+                f"{prefix}.up_proj": _ExpertLinearView(self.gate_up_proj.data[m, i:])}
+
+    def _dense_view(self, m, key):
+        i, k = self.intermediate_dim, self.intermediate_dim // BLOCK
+        return {"gate_proj.weight": lambda: self.gate_up_proj.data[m, :i],
+                "up_proj.weight": lambda: self.gate_up_proj.data[m, i:],
+                "down_proj.weight": lambda: self.down_proj.data[m],
+                "gate_proj.weight_scale_inv": lambda: self.gate_up_proj_scale_inv[m, :k],
+                "up_proj.weight_scale_inv": lambda: self.gate_up_proj_scale_inv[m, k:],
+                "down_proj.weight_scale_inv": lambda: self.down_proj_scale_inv[m]}[key]()
+
+    def _has_dense(self):
+        return isinstance(getattr(self, "gate_up_proj", None), torch.Tensor)
+
+    def load_expert_tensor(self, m, key, value, threads_per_block=512, bytes_per_thread=8):
+        """Takes one per-expert checkpoint tensor: a dense weight or scale
+        (copied into the fused parameter) or a stream buffer."""
+        if key in _STREAM_KEYS:
+            self.add_expert_stream(m, key, value, threads_per_block, bytes_per_thread)
+            return
+        if key.endswith(".weight") and not self._has_dense():
+            raise ValueError(f"expert {m}: dense {key} after the experts were compressed")
+        dst = self._dense_view(m, key)
+        if dst.shape != value.shape:
+            raise ValueError(f"expert {m} {key}: shape {tuple(value.shape)}, expected {tuple(dst.shape)}")
+        dst.copy_(value.to(dst.dtype))
+
+    def add_expert_stream(self, m, key, value, threads_per_block=512, bytes_per_thread=8):
+        """Registers one stream buffer of expert m; once every expert has its
+        `encoded` buffer the dense parameters are dropped."""
+        if not 0 <= m < self.num_experts:
+            raise ValueError(f"expert {m} out of range")
+        self.threads_per_block, self.bytes_per_thread = threads_per_block, bytes_per_thread
+        if key == "split_positions":
+            want = [self.hidden_dim * self.intermediate_dim, 2 * self.hidden_dim * self.intermediate_dim]
+            got = [int(x) for x in (value.tolist() if isinstance(value, torch.Tensor) else value)]
+            if got != want:
+                raise ValueError(f"expert {m}: split positions {got}, expected {want} (down, gate, up)")
+            return
+        self.register_buffer(f"ecf8_{m}_{key}", value)
+        if key == "encoded":
+            self.compressed.add(m)
+            if len(self.compressed) == self.num_experts and self._has_dense():
+                del self.gate_up_proj
+                del self.down_proj
+
+    def _stream(self, m):
+        s = {k: getattr(self, f"ecf8_{m}_{k}") for k in _STREAM_KEYS if k != "split_positions"}
+        s["decode_table"] = getattr(self, f"ecf8_{m}_decode_table", None)
+        return s
+
+    # -- state dict in the per-expert checkpoint layout -------------------------
+    def _save_to_state_dict(self, destination, prefix, keep_vars):
+        for m in range(self.num_experts):
+            if m in self.compressed:
+                for k in _STREAM_KEYS:
+                    if k == "split_positions":
+                        hi = self.hidden_dim * self.intermediate_dim
+                        destination[f"{prefix}{m}.{k}"] = torch.tensor([hi, 2 * hi], dtype=torch.int64)
+                    else:
+                        destination[f"{prefix}{m}.{k}"] = getattr(self, f"ecf8_{m}_{k}")
+                keys = [k for k in _DENSE_KEYS if k.endswith("_scale_inv")]
+            else:
+                keys = _DENSE_KEYS
+            for k in keys:
+                t = self._dense_view(m, k)
+                destination[f"{prefix}{m}.{k}"] = t if keep_vars else t.detach()
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                              error_msgs):
+        for name in list(state_dict):
+            if not name.startswith(prefix):
+                continue
+            rest = name[len(prefix):]
+            head, _, key = rest.partition(".")
+            if head.isdigit() and (key in _STREAM_KEYS or key in _DENSE_KEYS):
+                self.load_expert_tensor(int(head), key, state_dict[name])
+            elif not rest.startswith("ecf8_"):
+                unexpected_keys.append(name)
+
+    # -- forward ----------------------------------------------------------------
+    def expert_weights(self, experts):
+        """[(gate_up [2I, H], down [H, I])] e4m3 for the given experts: views of
+        the dense parameters, or of their decoded streams (one batched launch)."""
+        if not self.compressed:
+            return [(self.gate_up_proj[m], self.down_proj[m]) for m in experts]
+        from .run import TensorManager, build_decode_table, decode_streams
+        h, i = self.hidden_dim, self.intermediate_dim
+        per = 3 * h * i
+        pad = (per + 255) & ~255
+        dev = getattr(self, f"ecf8_{experts[0]}_encoded").device if experts else None
+        if not experts:
+            return []
+        fresh = False
+        for m in experts:
+            if getattr(self, f"ecf8_{m}_decode_table", None) is None:
+                self.register_buffer(f"ecf8_{m}_decode_table",
+                                     build_decode_table(getattr(self, f"ecf8_{m}_luts")), persistent=False)
+                fresh = True
+        scratch = TensorManager.get_tensor(dev, len(experts) * pad)
+        outs = [scratch[j * pad:j * pad + per] for j in range(len(experts))]
+        decode_streams([self._stream(m) for m in experts], [o.view(torch.uint8) for o in outs],
+                       self.threads_per_block, self.bytes_per_thread, overlap_previous=not fresh)
+        return [(o[h * i:].view(2 * i, h), o[:h * i].view(h, i)) for o in outs]
+
+    def forward(self, hidden_states, top_k_index, top_k_weights):
+        final = torch.zeros_like(hidden_states)
+        with torch.no_grad():
+            mask = F.one_hot(top_k_index, num_classes=self.num_experts).permute(2, 1, 0)
+            hit = torch.greater(mask.sum(dim=(-1, -2)), 0).nonzero()[:, 0].tolist()
+        for m, (gate_up, down) in zip(hit, self.expert_weights(hit)):
+            top_k_pos, token_idx = torch.where(mask[m])
+            gate, up = fp8_linear(hidden_states[token_idx], gate_up, self.gate_up_proj_scale_inv[m]).chunk(2, dim=-1)
+            cur = fp8_linear(self.act_fn(gate) * up, down, self.down_proj_scale_inv[m])
+            cur = cur * top_k_weights[token_idx, top_k_pos, None]
+            final.index_add_(0, token_idx, cur.to(final.dtype))
+        return final
+
+    def extra_repr(self):
+        return (f"num_experts={self.num_experts}, hidden={self.hidden_dim}, intermediate={self.intermediate_dim}, "
+                f"e4m3 128x128, compressed={len(self.compressed)}")
+
+
+def fused_experts_owner(model, name):
+    """(Fp8FusedExperts module, expert index, key) when `name` addresses one
+    expert's tensor inside a fused expert block ("...experts.M.key"), else None."""
+    parts = name.split(".")
+    mod = model
+    for j, part in enumerate(parts):
+        if isinstance(mod, Fp8FusedExperts):
+            if part.isdigit() and j + 1 < len(parts):
+                return mod, int(part), ".".join(parts[j + 1:])
+            return None
+        mod = getattr(mod, part, None)
+        if mod is None or not isinstance(mod, nn.Module):
+            return None
+    return None
+
+
+def replace_fused_experts_with_fp8(model, device=None):
+    """Swaps every fused expert block (a module with 3-D `gate_up_proj` /
+    `down_proj`, e.g. Qwen3MoeExperts) for an Fp8FusedExperts of the same
+    shape (uninitialised).  Returns the swapped names."""
+    names = []
+    for name, mod in list(model.named_modules()):
+        gu = getattr(mod, "gate_up_proj", None)
+        if isinstance(mod, Fp8FusedExperts) or not isinstance(gu, torch.Tensor) or gu.dim() != 3:
+            continue
+        parent = model
+        parts = name.split(".")
+        for p in parts[:-1]:
+            parent = getattr(parent, p)
+        e, two_i, h = gu.shape
+        dev = device if device is not None else gu.device
+        setattr(parent, parts[-1], Fp8FusedExperts(e, h, two_i // 2, mod.act_fn, dev))
+        names.append(name)
+    return names
 
 
 def quantize_block128(w):
@@ -151,6 +383,7 @@ def fp8_model_from_config(config, device="cuda", seed=None, std=0.02, dtype=torc
     with torch.device(device):
         model = AutoModelForCausalLM.from_config(config, dtype=dtype)
     replace_linears_with_fp8(model, device)
+    replace_fused_experts_with_fp8(model, device)
     model.eval()
     if seed is not None:
         with torch.no_grad():
@@ -163,6 +396,16 @@ def fp8_model_from_config(config, device="cuda", seed=None, std=0.02, dtype=torc
                     mod.weight.data.copy_(q)
                     mod.weight_scale_inv.copy_(s)
                     k += 1
+                elif isinstance(mod, Fp8FusedExperts):
+                    for m in range(mod.num_experts):
+                        for key, (o, i) in (("gate_proj", (mod.intermediate_dim, mod.hidden_dim)),
+                                            ("up_proj", (mod.intermediate_dim, mod.hidden_dim)),
+                                            ("down_proj", (mod.hidden_dim, mod.intermediate_dim))):
+                            g = torch.Generator(device=device).manual_seed(seed + k)
+                            q, s = quantize_block128(torch.randn(o, i, generator=g, device=device) * std)
+                            mod.load_expert_tensor(m, key + ".weight", q)
+                            mod.load_expert_tensor(m, key + ".weight_scale_inv", s)
+                            k += 1
             for name, p in model.named_parameters(recurse=True):
                 if p.dtype == torch.float8_e4m3fn:
                     continue

@@ -380,6 +380,12 @@ def _module_at(model, tensor_name):
 
 
 def _load_one(model, tensor_name, tensor_value, params, buffers, state_keys, pattern_dict, tpb, bpt):
+    from .fp8_model import fused_experts_owner
+    fused = fused_experts_owner(model, tensor_name)
+    if fused is not None:  # one expert's tensor of a fused expert block (per-expert checkpoint keys)
+        owner, m, key = fused
+        owner.load_expert_tensor(m, key, tensor_value, tpb, bpt)
+        return
     if tensor_name in state_keys:
         target = params.get(tensor_name)
         if target is None:
