@@ -502,7 +502,7 @@ def run_ours(args, rank, world, dev):
         cfg = {
             "workload": (f"config 5: Qwen3-235B-A22B-shaped MoE decode, {args.moe_layers} layers, 128 experts "
                          f"x 18,874,368 weights split {QWEN3_235B_EXPERTS // world}/GPU + attention replica "
-                         "(71,303,168) per GPU, one batched launch per layer (up to 128 streams per launch)"),
+                         "(71,303,168) per GPU, one batched launch per layer (up to 256 streams per launch)"),
             "parallelism": f"expert-sharded x{world}, no data-path collective",
             "scaling_note": ("all 128 experts of every layer are split over the ranks (fixed total); each rank "
                              "also decodes a replica of the attention stream, counted in value"),

@@ -21,7 +21,7 @@ NOALLOC_MAX_ELEMENTS = 268435456
 ABI_VERSION = 7
 TABLE_BYTES = 86544  # prepared decode table (ecf8_build_table)
 MAX_LUTS = 18
-MAX_BATCH = 128
+MAX_BATCH = 256
 DECODE_OVERLAP_PREVIOUS = 1  # ecf8_decode_batch_flags: may start while the stream's previous kernel runs
 THREADS_PER_BLOCK = 512
 BYTES_PER_THREAD = 8

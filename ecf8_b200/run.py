@@ -173,7 +173,7 @@ def decode_stream(luts, encoded, packed_other_4bits, output_positions, gaps, out
 
 def decode_streams(streams, outs, threads_per_block=512, bytes_per_thread=8, stream=None,
                    overlap_previous=False):
-    """Decodes several streams with one persistent launch per 128 streams.
+    """Decodes several streams with one persistent launch per 256 streams.
     `streams` is a list of dicts with the five stream buffers (and optionally
     "decode_table"); `outs` the matching output tensors.  All on one device.
     overlap_previous as in decode_stream."""

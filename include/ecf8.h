@@ -45,7 +45,7 @@ extern "C" {
 #define ECF8_BYTES_PER_THREAD 8    /* window size in bytes (decode.cu:5) */
 #define ECF8_THREADS_PER_BLOCK 512 /* windows per group (compress.py:7) */
 #define ECF8_MAX_LUTS 18           /* row 0 + 16 prefix rows + length row */
-#define ECF8_MAX_BATCH 128         /* streams per ecf8_decode_batch launch */
+#define ECF8_MAX_BATCH 256         /* streams per ecf8_decode_batch launch */
 #define ECF8_TABLE_BYTES 86544     /* prepared decode table (ecf8_build_table) */
 
 /* One stream of a batched decode; field meaning as in ecf8_decode(). */

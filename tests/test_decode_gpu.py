@@ -141,7 +141,7 @@ def test_batch_of_all_golden_streams(cuda_device):
 
 @pytest.mark.parametrize("overlap", [False, True])
 def test_batch_larger_than_one_launch(cuda_device, oracle_mod, overlap):
-    """300 streams: three launches per call; with overlap each may start while
+    """300 streams: two launches per call; with overlap the second may start while
     the one before it runs (their outputs are disjoint, their inputs were
     written before the call)."""
     from ecf8_b200.run import decode_streams
