@@ -24,6 +24,7 @@ from .run import (  # noqa: F401
     build_decode_table,
     decode_stream,
     decode_streams,
+    enable_decode_prefetch,
     get_dfloat_model_name_or_path,
     get_hook,
     load_and_replace_tensors,

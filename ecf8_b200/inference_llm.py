@@ -127,6 +127,8 @@ def main(argv=None):
     ap.add_argument("--compressed_only", action="store_true", help="compressed arm only")
     ap.add_argument("--keep", type=int, default=4, help="steps whose full logits are compared")
     ap.add_argument("--warm_tokens", type=int, default=None, help="warm-up generation length (default: num_tokens)")
+    ap.add_argument("--prefetch", action="store_true",
+                    help="compressed arm: decode each layer one layer ahead on a side stream")
     ap.add_argument("--fp8_matmul", choices=["auto", "dequant"], default="auto",
                     help="auto: block-scaled FP8 GEMM on e4m3 weights; dequant: bf16 expansion + bf16 matmul")
     args = ap.parse_args(argv)
@@ -158,6 +160,10 @@ def main(argv=None):
     if not args.no_compress:
         t1 = time.time()
         compress_model_in_place(model)
+        if args.prefetch:
+            from .run import enable_decode_prefetch
+            enable_decode_prefetch(model)
+        line["decode_prefetch"] = bool(args.prefetch)
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
         TensorManager.clear_device()

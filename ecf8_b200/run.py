@@ -299,32 +299,124 @@ def inject_weights(module, reconstructed):
                 raise ValueError(f"Unsupported module type: {type(sub)}")
 
 
+def _block_table(module):
+    """The block's prepared decode table, built on first use on the current
+    stream and kept as a non-persistent buffer (not part of the checkpoint).
+    Returns (table, built now)."""
+    device = module.encoded.device
+    table = getattr(module, "ecf8_decode_table", None)
+    if table is not None and table.device == device:
+        return table, False
+    table = build_decode_table(module.luts)
+    module.register_buffer("ecf8_decode_table", table, persistent=False)
+    return table, True
+
+
+class _Prefetch:
+    """Per-device state of the prefetching hook: a side stream, two scratch
+    buffers used in turn by consecutive blocks, and the decodes in flight."""
+
+    def __init__(self, device):
+        self.device = device
+        self.side = torch.cuda.Stream(device)
+        self.bufs = [None, None]
+        self.pending = {}  # module -> (buffer index, event after its decode)
+
+    def buffer(self, i, n):
+        b = self.bufs[i]
+        if b is None or b.numel() < n:
+            b = torch.empty(n, dtype=torch.float8_e4m3fn, device=self.device)
+            self.bufs[i] = b
+        return b[:n]
+
+
+_PREFETCH = {}
+
+
+def _n_elements(module):
+    return module.packed_other_4bits.numel() * 2
+
+
+def _decode_block(module, out, tpb, bpt, stream=None):
+    table, fresh = _block_table(module)
+    # The block's buffers and an existing table are written only at load
+    # time, so the decode may start while the previous kernel on the stream
+    # runs (it overwrites the scratch only after that kernel); right after
+    # building the table it may not.
+    decode_stream(module.luts, module.encoded, module.packed_other_4bits, module.output_positions,
+                  module.gaps, out, tpb, bpt, table=table, overlap_previous=not fresh, stream=stream)
+
+
 def get_hook(threads_per_block, bytes_per_thread):
     """forward_pre_hook that decodes a block's ECF8 stream into the device's
-    shared scratch and injects the weight views (run.py:84-155)."""
+    shared scratch and injects the weight views (run.py:84-155).  With
+    enable_decode_prefetch() on the model, the block's weights were decoded
+    ahead on a side stream and the hook also starts the next block's decode."""
 
     def decode_hook(module, _):
-        n_elements = module.packed_other_4bits.numel() * 2
-        device = module.encoded.device
-        reconstructed = TensorManager.get_tensor(device, n_elements)
-        # The decode table depends on the LUTs only: derived on the first
-        # decode on a device and kept as a non-persistent buffer (it is not
-        # part of the checkpoint).
-        table = getattr(module, "ecf8_decode_table", None)
-        fresh = table is None or table.device != device
-        if fresh:
-            table = build_decode_table(module.luts)
-            module.register_buffer("ecf8_decode_table", table, persistent=False)
-        # The block's buffers and an existing table are written only at load
-        # time, so the decode may start while the previous layer's last
-        # kernel runs (it overwrites the shared scratch only after that
-        # kernel); right after building the table it may not.
-        decode_stream(module.luts, module.encoded, module.packed_other_4bits, module.output_positions,
-                      module.gaps, reconstructed, threads_per_block, bytes_per_thread, table=table,
-                      overlap_previous=not fresh)
+        nxt = getattr(module, "_ecf8_next", None)
+        if nxt is not None:
+            _prefetch_hook(module, nxt, threads_per_block, bytes_per_thread)
+            return
+        reconstructed = TensorManager.get_tensor(module.encoded.device, _n_elements(module))
+        _decode_block(module, reconstructed, threads_per_block, bytes_per_thread)
         inject_weights(module, reconstructed)
 
     return decode_hook
+
+
+def _prefetch_hook(module, nxt, tpb, bpt):
+    device = module.encoded.device
+    st = _PREFETCH.get(device)
+    if st is None:
+        st = _PREFETCH[device] = _Prefetch(device)
+    cur = torch.cuda.current_stream(device)
+    if module in st.pending:  # decoded ahead: wait for that decode on this stream
+        slot, ready = st.pending.pop(module)
+        cur.wait_event(ready)
+        buf = st.buffer(slot, _n_elements(module))
+    else:  # not decoded ahead (first block of a forward, or another order): decode here
+        used = {s for s, _ in st.pending.values()}
+        slot = 0 if 0 not in used else 1
+        st.pending = {m: v for m, v in st.pending.items() if v[0] != slot}
+        buf = st.buffer(slot, _n_elements(module))
+        _decode_block(module, buf, tpb, bpt)
+    inject_weights(module, buf)
+    # The next block goes into the other buffer once everything enqueued so far
+    # on this stream is done (that buffer was read by the block before this one).
+    other = 1 - slot
+    st.pending = {m: v for m, v in st.pending.items() if v[0] != other}
+    nbuf = st.buffer(other, _n_elements(nxt))
+    done = torch.cuda.Event()
+    done.record(cur)
+    st.side.wait_event(done)
+    with torch.cuda.stream(st.side):
+        _, fresh = _block_table(nxt)
+        decode_stream(nxt.luts, nxt.encoded, nxt.packed_other_4bits, nxt.output_positions, nxt.gaps, nbuf,
+                      tpb, bpt, table=nxt.ecf8_decode_table, stream=st.side)
+        ready = torch.cuda.Event()
+        ready.record(st.side)
+    st.pending[nxt] = (other, ready)
+
+
+def enable_decode_prefetch(model, enable=True):
+    """Decode-ahead mode of the forward-pre-hook: each hooked block, in module
+    order (the forward order of decoder layers and DiT blocks), starts the
+    next block's decode on a side stream into the second of two per-device
+    scratch buffers, and its own hook only waits for the decode started one
+    block earlier.  The decode then runs while the GPU would otherwise wait
+    for the host to launch the current block's kernels (eager generation is
+    launch-bound at small batch); decoded bytes, and so outputs, are the same
+    as with the plain hook.  Uses two scratch buffers of the largest block
+    instead of one.  The last block prefetches the first (the next forward).
+    Returns the number of hooked blocks.  enable=False restores the plain hook."""
+    blocks = [m for m in model.modules() if "encoded" in m._buffers and "luts" in m._buffers
+              and any(getattr(h, "__name__", "") == "decode_hook" for h in m._forward_pre_hooks.values())]
+    for i, m in enumerate(blocks):
+        m._ecf8_next = blocks[(i + 1) % len(blocks)] if enable else None
+    if not enable:
+        _PREFETCH.clear()
+    return len(blocks)
 
 
 # ---------------------------------------------------------------------------

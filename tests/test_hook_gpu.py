@@ -161,3 +161,30 @@ def test_reference_launcher_caches_tables_and_survives_reused_lut_memory(cuda_de
     assert run(a)
     _decode.clear_cache()
     assert not _decode._tables
+
+
+def test_decode_prefetch_mode_matches_uncompressed(cuda_device, tmp_path):
+    """enable_decode_prefetch: each block's hook decodes the next block on a
+    side stream into the second scratch buffer; outputs stay bit-identical
+    over repeated forwards, and turning it off restores the plain hook."""
+    from ecf8_b200 import enable_decode_prefetch, load_and_replace_tensors
+    from ecf8_b200.run import TensorManager
+    dev = cuda_device
+    ref = Tiny(dev, n=4)
+    x = torch.randn(8, 256, device=dev)
+    y_ref = ref(x)
+    save_compressed(ref, str(tmp_path))
+    model = Tiny(dev, seed=9, n=4)
+    cfg = {"threads_per_block": 512, "bytes_per_thread": 8,
+           "pattern_dict": json.load(open(tmp_path / "pattern_dict.json"))}
+    load_and_replace_tensors(model, str(tmp_path), cfg)
+    model.to(dev)
+    TensorManager.clear_device()
+    assert enable_decode_prefetch(model) == 4
+    for _ in range(4):
+        assert torch.equal(model(x), y_ref)
+    # the blocks alternate between two buffers
+    ptrs = [blk.down_proj.weight.data_ptr() for blk in model.layers]
+    assert len(set(ptrs)) == 2
+    enable_decode_prefetch(model, enable=False)
+    assert torch.equal(model(x), y_ref)
