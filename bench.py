@@ -786,6 +786,21 @@ def reference_gpu_kernel(oracle, s, n, want, args):
 # ---------------------------------------------------------------------------
 
 def main():
+    # Stdout carries the one JSON line only: whatever libraries print there
+    # (NCCL's version banner at communicator creation, for one) goes to stderr.
+    out_fd = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        line = _main()
+    finally:
+        sys.stdout.flush()
+        os.dup2(out_fd, 1)
+        os.close(out_fd)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+def _main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -809,9 +824,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        if rank == 0:
-            print(json.dumps(run_reference(args)), flush=True)
-        return
+        return run_reference(args) if rank == 0 else None
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if under_torchrun():
@@ -827,8 +840,7 @@ def main():
             import torch.distributed as dist
             dist.barrier()
             dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(line), flush=True)
+    return line if rank == 0 else None
 
 
 if __name__ == "__main__":
