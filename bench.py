@@ -162,16 +162,26 @@ def peak_hbm():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic(name):
-    """Per-launch DRAM bytes recorded in profiles/<name> ("dram_bytes_per_launch: X")."""
+def profiled_traffic(name, per_launch_bytes):
+    """DRAM bytes per launch from the ncu summary profiles/<name>: its
+    captured launch's "dram_bytes_per_launch" scaled by this bench's
+    algorithmic bytes per launch over the captured launch's
+    ("algorithmic_bytes_per_launch"; the decode's traffic grows in proportion
+    to the bytes it decodes).  None without a summary."""
     p = os.path.join(ROOT, "profiles", name)
+    vals = {}
     try:
         for line in open(p):
-            if line.strip().startswith("dram_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].split()[0])
+            k, _, v = line.strip().partition(":")
+            if k in ("dram_bytes_per_launch", "algorithmic_bytes_per_launch") and v.strip():
+                vals[k] = float(v.split()[0])
     except OSError:
-        pass
-    return None
+        return None
+    if "dram_bytes_per_launch" not in vals:
+        return None
+    if "algorithmic_bytes_per_launch" not in vals:
+        return vals["dram_bytes_per_launch"]
+    return round(vals["dram_bytes_per_launch"] / vals["algorithmic_bytes_per_launch"] * per_launch_bytes)
 
 
 def max_over_ranks(x, world):
@@ -469,7 +479,7 @@ def run_ours(args, rank, world, dev):
     per_launch_bytes = algo / n_launch_groups
     achieved = per_launch_bytes / (mean_launch_ms * 1e-3) / 1e9
     traffic = profiled_traffic("decode_kernel_qwen3_8b_layer.md" if workload == "config2"
-                               else "decode_kernel_config5_layer.md")
+                               else "decode_kernel_config5_layer.md", per_launch_bytes)
     if steady is not None:
         steady["roofline_frac"] = round(per_launch_bytes / (steady["mean_launch_us"] * 1e-6) / 1e9 / peak, 4)
         steady["value"] = round(total_elems / (steady["ms_per_step"] * 1e-3) / 1e9, 2)

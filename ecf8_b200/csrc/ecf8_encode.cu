@@ -91,19 +91,17 @@ __global__ void __launch_bounds__(kThreads) chunk_bits_kernel(const uint8_t* __r
                                                               const __grid_constant__ CodeTable T,
                                                               unsigned long long* __restrict__ chunk) {
     __shared__ uint32_t red[kThreads / 32];
-    __shared__ uint32_t red2[kThreads / 32];
     const long long i0 = (long long)blockIdx.x * kChunk + (long long)threadIdx.x * kPerThread;
     int sym[kPerThread];
     load16(ex, n, i0, sym);
-    uint32_t s = 0, bad = 0;
+    // One reduction for both sums: a chunk has at most 4096 x 16 = 2^16 code
+    // bits (bits 16..0) and 4096 invalid exponents (bits 29..17).
+    uint32_t v = 0;
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j) {
-        s += sym_bits(T, sym[j]);
-        bad += sym_invalid(T, sym[j]);
-    }
-    s = block_sum(s, red);
-    bad = block_sum(bad, red2);
-    if (threadIdx.x == 0) chunk[blockIdx.x] = (unsigned long long)s | ((unsigned long long)bad << kInvalidShift);
+    for (int j = 0; j < kPerThread; ++j) v += sym_bits(T, sym[j]) + (sym_invalid(T, sym[j]) << 17);
+    v = block_sum(v, red);
+    if (threadIdx.x == 0)
+        chunk[blockIdx.x] = (unsigned long long)(v & 0x1ffffu) | ((unsigned long long)(v >> 17) << kInvalidShift);
 }
 
 // Exclusive scan of the chunk sums in place (chunk[c] becomes the first bit of
