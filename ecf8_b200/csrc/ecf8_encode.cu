@@ -72,16 +72,34 @@ __device__ __forceinline__ void load16(const uint8_t* ex, long long n, long long
     }
 }
 
-__device__ __forceinline__ uint32_t sym_bits(const CodeTable& T, int s) {
-    return s < 0 ? 0u : (uint32_t)T.bits[s & 15];
+// The code table in shared memory: lanes look up different symbols, which
+// the kernel-parameter (constant) bank would serve one address at a time.
+struct SmemTable {
+    uint32_t val[16];
+    uint32_t bits[16];
+};
+
+__device__ __forceinline__ void load_table(SmemTable& t, const CodeTable& T) {
+    if (threadIdx.x < 16) {
+        t.val[threadIdx.x] = T.val[threadIdx.x];
+        t.bits[threadIdx.x] = T.bits[threadIdx.x];
+    }
+    __syncthreads();
 }
 
-// 1 for an exponent the code table cannot encode: a byte above 15 or a symbol
-// whose code length is 0.  Such exponents encode as nothing (their masked
-// length is 0), so every offset stays inside the planned stream; the plan
-// counts them and emit writes nothing when the count is not 0.
-__device__ __forceinline__ uint32_t sym_invalid(const CodeTable& T, int s) {
-    return s >= 0 && (s > 15 || T.bits[s & 15] == 0) ? 1u : 0u;
+__device__ __forceinline__ uint32_t sym_bits(const SmemTable& t, int s) {
+    return s < 0 ? 0u : t.bits[s & 15];
+}
+
+// Code bits of symbol s (bits 16..0) plus 1 << 17 for an exponent the code
+// table cannot encode: a byte above 15 or a symbol whose code length is 0.
+// Such exponents encode as nothing (their masked length is 0), so every
+// offset stays inside the planned stream; the plan counts them and emit
+// writes nothing when the count is not 0.
+__device__ __forceinline__ uint32_t sym_bits_and_invalid(const SmemTable& t, int s) {
+    if (s < 0) return 0u;
+    const uint32_t b = t.bits[s & 15];
+    return b | ((b == 0u || s > 15) ? (1u << 17) : 0u);
 }
 
 constexpr int kInvalidShift = 32;  // chunk sums: code bits in the low half, invalid exponents in the high half
@@ -91,6 +109,8 @@ __global__ void __launch_bounds__(kThreads) chunk_bits_kernel(const uint8_t* __r
                                                               const __grid_constant__ CodeTable T,
                                                               unsigned long long* __restrict__ chunk) {
     __shared__ uint32_t red[kThreads / 32];
+    __shared__ SmemTable t;
+    load_table(t, T);
     const long long i0 = (long long)blockIdx.x * kChunk + (long long)threadIdx.x * kPerThread;
     int sym[kPerThread];
     load16(ex, n, i0, sym);
@@ -98,7 +118,7 @@ __global__ void __launch_bounds__(kThreads) chunk_bits_kernel(const uint8_t* __r
     // bits (bits 16..0) and 4096 invalid exponents (bits 29..17).
     uint32_t v = 0;
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j) v += sym_bits(T, sym[j]) + (sym_invalid(T, sym[j]) << 17);
+    for (int j = 0; j < kPerThread; ++j) v += sym_bits_and_invalid(t, sym[j]);
     v = block_sum(v, red);
     if (threadIdx.x == 0)
         chunk[blockIdx.x] = (unsigned long long)(v & 0x1ffffu) | ((unsigned long long)(v >> 17) << kInvalidShift);
@@ -189,13 +209,15 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(const uint8_t* __restric
                                                         uint32_t* __restrict__ gaps32,
                                                         uint64_t* __restrict__ op) {
     __shared__ uint32_t wsum[kThreads / 32];
+    __shared__ SmemTable t;
+    load_table(t, T);
     const long long c = blockIdx.x;
     const long long i0 = c * kChunk + (long long)threadIdx.x * kPerThread;
     int sym[kPerThread];
     load16(ex, n, i0, sym);
     uint32_t local = 0;
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j) local += sym_bits(T, sym[j]);
+    for (int j = 0; j < kPerThread; ++j) local += sym_bits(t, sym[j]);
     // block exclusive scan of per-thread bit counts
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t v = local;
@@ -236,8 +258,8 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(const uint8_t* __restric
 #pragma unroll
     for (int j = 0; j < kPerThread; ++j) {
         if (sym[j] < 0) break;
-        const uint32_t len = T.bits[sym[j] & 15];
-        const uint32_t code = T.val[sym[j] & 15];
+        const uint32_t len = t.bits[sym[j] & 15];
+        const uint32_t code = t.val[sym[j] & 15];
         const long long i = i0 + j;
         // window / group bookkeeping (utils.py:392-406)
         const unsigned long long ps = (j == 0) ? prev_start : last_start;
