@@ -404,10 +404,14 @@ def enable_decode_prefetch(model, enable=True):
     order (the forward order of decoder layers and DiT blocks), starts the
     next block's decode on a side stream into the second of two per-device
     scratch buffers, and its own hook only waits for the decode started one
-    block earlier.  The decode then runs while the GPU would otherwise wait
-    for the host to launch the current block's kernels (eager generation is
-    launch-bound at small batch); decoded bytes, and so outputs, are the same
-    as with the plain hook.  Uses two scratch buffers of the largest block
+    block earlier.  The decode can then run while the GPU would otherwise wait
+    for the host to launch the current block's kernels; decoded bytes, and so
+    outputs, are the same as with the plain hook.  It pays only where the
+    forward leaves the GPU idle between launches: a decode holds every SM
+    while it runs, so it does not share them with the block's own kernels,
+    and the mode costs some host time per block (the batch-16 Qwen3-8B
+    generation of the benchmark, whose step keeps the GPU busy, runs slower
+    with it: 0.838 against 0.889 of the uncompressed tokens/s).  Uses two scratch buffers of the largest block
     instead of one.  The last block prefetches the first (the next forward).
     Returns the number of hooked blocks.  enable=False restores the plain hook."""
     blocks = [m for m in model.modules() if "encoded" in m._buffers and "luts" in m._buffers
