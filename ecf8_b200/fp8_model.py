@@ -262,27 +262,29 @@ class Fp8FusedExperts(nn.Module):
     # -- forward ----------------------------------------------------------------
     def expert_weights(self, experts):
         """[(gate_up [2I, H], down [H, I])] e4m3 for the given experts: views of
-        the dense parameters, or of their decoded streams (one batched launch)."""
-        if not self.compressed:
-            return [(self.gate_up_proj[m], self.down_proj[m]) for m in experts]
-        from .run import TensorManager, build_decode_table, decode_streams
-        h, i = self.hidden_dim, self.intermediate_dim
-        per = 3 * h * i
-        pad = (per + 255) & ~255
-        dev = getattr(self, f"ecf8_{experts[0]}_encoded").device if experts else None
-        if not experts:
-            return []
-        fresh = False
-        for m in experts:
-            if getattr(self, f"ecf8_{m}_decode_table", None) is None:
-                self.register_buffer(f"ecf8_{m}_decode_table",
-                                     build_decode_table(getattr(self, f"ecf8_{m}_luts")), persistent=False)
-                fresh = True
-        scratch = TensorManager.get_tensor(dev, len(experts) * pad)
-        outs = [scratch[j * pad:j * pad + per] for j in range(len(experts))]
-        decode_streams([self._stream(m) for m in experts], [o.view(torch.uint8) for o in outs],
-                       self.threads_per_block, self.bytes_per_thread, overlap_previous=not fresh)
-        return [(o[h * i:].view(2 * i, h), o[:h * i].view(h, i)) for o in outs]
+        the dense parameters, or of their decoded streams (the compressed ones
+        among them in one batched launch)."""
+        coded = [m for m in experts if m in self.compressed]
+        views = {m: (self.gate_up_proj[m], self.down_proj[m]) for m in experts if m not in self.compressed}
+        if coded:
+            from .run import TensorManager, build_decode_table, decode_streams
+            h, i = self.hidden_dim, self.intermediate_dim
+            per = 3 * h * i
+            pad = (per + 255) & ~255
+            dev = getattr(self, f"ecf8_{coded[0]}_encoded").device
+            fresh = False
+            for m in coded:
+                if getattr(self, f"ecf8_{m}_decode_table", None) is None:
+                    self.register_buffer(f"ecf8_{m}_decode_table",
+                                         build_decode_table(getattr(self, f"ecf8_{m}_luts")), persistent=False)
+                    fresh = True
+            scratch = TensorManager.get_tensor(dev, len(coded) * pad)
+            outs = [scratch[j * pad:j * pad + per] for j in range(len(coded))]
+            decode_streams([self._stream(m) for m in coded], [o.view(torch.uint8) for o in outs],
+                           self.threads_per_block, self.bytes_per_thread, overlap_previous=not fresh)
+            for m, o in zip(coded, outs):
+                views[m] = (o[h * i:].view(2 * i, h), o[:h * i].view(h, i))
+        return [views[m] for m in experts]
 
     def forward(self, hidden_states, top_k_index, top_k_weights):
         final = torch.zeros_like(hidden_states)

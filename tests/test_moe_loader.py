@@ -59,3 +59,16 @@ def test_expert_stream_split_positions_are_checked():
     m.add_expert_stream(0, "split_positions", torch.tensor([256 * 128, 2 * 256 * 128]))
     with pytest.raises(ValueError):
         m.add_expert_stream(0, "split_positions", torch.tensor([128, 256]))
+
+
+def test_partly_compressed_experts_keep_their_dense_weights():
+    """Streams for some experts only: the dense parameters stay (needed by
+    the others) and every expert's weights come from the right place."""
+    from ecf8_b200.fp8_model import Fp8FusedExperts
+    m = Fp8FusedExperts(4, 256, 128, torch.nn.functional.silu)
+    for k in ("luts", "packed_other_4bits", "output_positions", "gaps"):
+        m.add_expert_stream(1, k, torch.zeros(4, dtype=torch.uint8))
+    m.add_expert_stream(1, "encoded", torch.zeros(4, dtype=torch.uint8))
+    assert m.compressed == {1} and m._has_dense()
+    w = m.expert_weights([0, 2])
+    assert w[0][0].data_ptr() == m.gate_up_proj[0].data_ptr() and w[1][1].shape == (256, 128)
