@@ -314,20 +314,18 @@ def _block_table(module):
 
 class _Prefetch:
     """Per-device state of the prefetching hook: a side stream, two scratch
-    buffers used in turn by consecutive blocks, and the decodes in flight."""
+    buffers (each the size of the largest block, allocated once, so no buffer
+    is freed while a side-stream decode writes it) used in turn by
+    consecutive blocks, and the decodes in flight."""
 
-    def __init__(self, device):
+    def __init__(self, device, n_max):
         self.device = device
         self.side = torch.cuda.Stream(device)
-        self.bufs = [None, None]
+        self.bufs = [torch.empty(n_max, dtype=torch.float8_e4m3fn, device=device) for _ in range(2)]
         self.pending = {}  # module -> (buffer index, event after its decode)
 
     def buffer(self, i, n):
-        b = self.bufs[i]
-        if b is None or b.numel() < n:
-            b = torch.empty(n, dtype=torch.float8_e4m3fn, device=self.device)
-            self.bufs[i] = b
-        return b[:n]
+        return self.bufs[i][:n]
 
 
 _PREFETCH = {}
@@ -368,14 +366,17 @@ def get_hook(threads_per_block, bytes_per_thread):
 def _prefetch_hook(module, nxt, tpb, bpt):
     device = module.encoded.device
     st = _PREFETCH.get(device)
-    if st is None:
-        st = _PREFETCH[device] = _Prefetch(device)
+    if st is None or st.bufs[0].numel() < max(_n_elements(module), _n_elements(nxt)):
+        n_max = max([_n_elements(m) for m in _prefetch_blocks(module)] + [_n_elements(module), _n_elements(nxt)])
+        st = _PREFETCH[device] = _Prefetch(device, n_max)
     cur = torch.cuda.current_stream(device)
     if module in st.pending:  # decoded ahead: wait for that decode on this stream
         slot, ready = st.pending.pop(module)
         cur.wait_event(ready)
         buf = st.buffer(slot, _n_elements(module))
-    else:  # not decoded ahead (first block of a forward, or another order): decode here
+    else:  # not decoded ahead (first block of a forward, or another order): decode here,
+        # after every side-stream decode still writing either buffer
+        cur.wait_stream(st.side)
         used = {s for s, _ in st.pending.values()}
         slot = 0 if 0 not in used else 1
         st.pending = {m: v for m, v in st.pending.items() if v[0] != slot}
@@ -399,6 +400,10 @@ def _prefetch_hook(module, nxt, tpb, bpt):
     st.pending[nxt] = (other, ready)
 
 
+def _prefetch_blocks(module):
+    return getattr(module, "_ecf8_blocks", None) or [module]
+
+
 def enable_decode_prefetch(model, enable=True):
     """Decode-ahead mode of the forward-pre-hook: each hooked block, in module
     order (the forward order of decoder layers and DiT blocks), starts the
@@ -418,6 +423,7 @@ def enable_decode_prefetch(model, enable=True):
               and any(getattr(h, "__name__", "") == "decode_hook" for h in m._forward_pre_hooks.values())]
     for i, m in enumerate(blocks):
         m._ecf8_next = blocks[(i + 1) % len(blocks)] if enable else None
+        m._ecf8_blocks = blocks if enable else None
     if not enable:
         _PREFETCH.clear()
     return len(blocks)
