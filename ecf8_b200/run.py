@@ -422,8 +422,9 @@ def enable_decode_prefetch(model, enable=True):
     blocks = [m for m in model.modules() if "encoded" in m._buffers and "luts" in m._buffers
               and any(getattr(h, "__name__", "") == "decode_hook" for h in m._forward_pre_hooks.values())]
     for i, m in enumerate(blocks):
-        m._ecf8_next = blocks[(i + 1) % len(blocks)] if enable else None
-        m._ecf8_blocks = blocks if enable else None
+        # plain attributes: assigning a module through nn.Module would make it a child
+        object.__setattr__(m, "_ecf8_next", blocks[(i + 1) % len(blocks)] if enable else None)
+        object.__setattr__(m, "_ecf8_blocks", blocks if enable else None)
     if not enable:
         _PREFETCH.clear()
     return len(blocks)

@@ -180,7 +180,9 @@ def test_decode_prefetch_mode_matches_uncompressed(cuda_device, tmp_path):
     load_and_replace_tensors(model, str(tmp_path), cfg)
     model.to(dev)
     TensorManager.clear_device()
+    keys = list(model.state_dict())
     assert enable_decode_prefetch(model) == 4
+    assert list(model.state_dict()) == keys  # the block chain is not part of the module tree
     for _ in range(4):
         assert torch.equal(model(x), y_ref)
     # the blocks alternate between two buffers

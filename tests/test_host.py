@@ -88,3 +88,19 @@ def test_const_tables_cover_qwen3():
     assert r"lm_head" in get_default_no_split_pattern("LlamaForCausalLM")
     with pytest.raises(ValueError):
         get_fp8_pattern_dict("GPT2LMHeadModel")
+
+
+def test_decode_prefetch_chain_stays_out_of_the_module_tree():
+    import torch.nn as nn
+    from ecf8_b200.run import enable_decode_prefetch, get_hook
+    blocks = nn.ModuleList([nn.Linear(2, 2) for _ in range(3)])
+    for b in blocks:
+        b.register_buffer("encoded", torch.zeros(4, dtype=torch.uint8))
+        b.register_buffer("luts", torch.zeros(2, 256, dtype=torch.uint8))
+        b.register_forward_pre_hook(get_hook(512, 8))
+    keys = list(blocks.state_dict())
+    assert enable_decode_prefetch(blocks) == 3
+    assert list(blocks.state_dict()) == keys and len(list(blocks.modules())) == 4
+    assert blocks[2]._ecf8_next is blocks[0]
+    enable_decode_prefetch(blocks, enable=False)
+    assert blocks[0]._ecf8_next is None
