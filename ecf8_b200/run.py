@@ -356,9 +356,25 @@ def get_hook(threads_per_block, bytes_per_thread):
         if nxt is not None:
             _prefetch_hook(module, nxt, threads_per_block, bytes_per_thread)
             return
-        reconstructed = TensorManager.get_tensor(module.encoded.device, _n_elements(module))
-        _decode_block(module, reconstructed, threads_per_block, bytes_per_thread)
-        inject_weights(module, reconstructed)
+        device = module.encoded.device
+        reconstructed = TensorManager.get_tensor(device, _n_elements(module))
+        table, fresh = _block_table(module)
+        key = (reconstructed.data_ptr(), table.data_ptr()) + tuple(module._buffers[k].data_ptr() for k in STREAM_BUFFERS)
+        cached = module.__dict__.get("_ecf8_launch")
+        if fresh or cached is None or cached[0] != key:
+            # First decode of this block (or its buffers or the scratch moved):
+            # checked launch, views injected, launch descriptor kept.
+            _decode_block(module, reconstructed, threads_per_block, bytes_per_thread)
+            inject_weights(module, reconstructed)
+            s = {k: module._buffers[k] for k in STREAM_BUFFERS}
+            module.__dict__["_ecf8_launch"] = (key, (_lib.Ecf8Stream * 1)(_stream_struct(s, reconstructed, table)))
+            return
+        # Later decodes: the same launch from the kept descriptor; the injected
+        # views already point at this scratch.
+        st = _lib.lib().ecf8_decode_batch_flags(cached[1], 1, threads_per_block, bytes_per_thread,
+                                                _lib.DECODE_OVERLAP_PREVIOUS,
+                                                torch.cuda.current_stream(device).cuda_stream)
+        _lib.check(st, "ecf8_decode_batch_flags")
 
     return decode_hook
 
