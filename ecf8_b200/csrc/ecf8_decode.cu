@@ -28,8 +28,9 @@
 //    each run in the warp's output-ordered nibble buffer.
 //  * Loads straight into registers.  A round's bitstream (16 bytes + 4 bytes
 //    of look-ahead per lane) and gap byte are loaded into registers while the
-//    previous round is placed and merged; its packed sign+mantissa nibbles
-//    are loaded while it decodes.
+//    previous round is placed and merged; the packed sign+mantissa nibbles a
+//    round's merge needs are loaded right after its decode, so they are not
+//    live (holding registers) during the decode loop.
 //  * Merge in whole-warp steps.  Once the nibble buffer holds 512 elements
 //    past the merge cursor, each lane merges one 16-element chunk per step
 //    (byte-permute/logic ops) and writes it with one 16-byte store; what is
@@ -640,7 +641,7 @@ __device__ __forceinline__ void load_round(RoundIn& in, const DevStream& d, long
 
 // Packed words of chunks C + lane + 32k (k < 4) of the output at `base`,
 // those below `climit` (chunks whose 16 elements lie below n_elements); the
-// merge steps of the next round use them.
+// round's merge steps use them.
 __device__ __forceinline__ void prefetch_packed(uint2 (&pw)[4], const DevStream& d, unsigned long long base,
                                                 uint32_t C, uint32_t climit, int lane) {
     if (d.packed_vec) {
@@ -731,7 +732,9 @@ __device__ __forceinline__ uint32_t chunk_limit(const DevStream& d, unsigned lon
 // all are relative to `base`, the output position (16-aligned) of the
 // range's first chunk.  A group that does not start where the previous one
 // ended (a stream the reference compressor did not write) flushes the buffer
-// and starts a new range.  Only __syncwarp orders the lanes.
+// and starts a new range.  Only __syncwarp orders the lanes.  Values needed
+// only after the decode (the packed words, the next group's range) are
+// loaded after it, so the decode loop has the registers to itself.
 __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int ga, int gb, int lane, Mul M) {
     uint32_t* obuf = W.obuf;
     const uint32_t lane_s = (uint32_t)__cvta_generic_to_shared(W.slot + lane);
@@ -740,8 +743,8 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int ga, int
     uint2 pw[4];
     unsigned long long base = 0;
     uint32_t P = 0, head = 0, re = 0, climit = 0, C = 0;
-    // The first round's input and the first packed words are loaded while the
-    // CTA sets up the stream's tables (all warps take part; ends with a barrier).
+    // The first round's input is loaded while the CTA sets up the stream's
+    // tables (all warps take part; ends with a barrier).
     if (have) {
         const GroupRange rg = group_range(d, ga);
         load_round(in, d, (long long)ga * kGroupBytes, d.gaps + (long long)ga * kGapStage, lane);
@@ -749,7 +752,6 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int ga, int
         P = head = (uint32_t)(rg.start - base);
         re = (uint32_t)(rg.end - base);
         climit = chunk_limit(d, base);
-        prefetch_packed(pw, d, base, 0, climit, lane);
     }
     setup_stream(S, d);
     // Under programmatic dependent launch (ECF8_DECODE_OVERLAP_PREVIOUS) the
@@ -761,7 +763,6 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int ga, int
 
     int g = ga, r = 0;
     long long lo = (long long)ga * kGroupBytes;
-    GroupRange rn = g + 1 < gb ? group_range(d, g + 1) : GroupRange{0, 0};
 #pragma unroll 1
     for (;;) {
         // --- decode this lane's window pair ---
@@ -770,6 +771,7 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int ga, int
             count = decode_run(S, lane_s, __byte_perm(in.w0, 0, 0x0123), __byte_perm(in.w1, 0, 0x0123),
                                __byte_perm(in.w2, 0, 0x0123), __byte_perm(in.w3, 0, 0x0123),
                                __byte_perm(in.w4, 0, 0x0123), in.gap >> 4, M);
+        prefetch_packed(pw, d, base, C, climit, lane);
         // --- the next round's input: the group's next round, else the next group's first ---
         const bool next_in_group = r + 1 < kRounds && lo + kRoundBytes < d.n_bytes;
         const int gn = next_in_group ? g : g + 1;
@@ -808,9 +810,8 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int ga, int
             // The next group continues this range if it starts where this
             // group ended (always, for a stream the reference compressor
             // wrote); otherwise the range ends here and a new one begins.
-            const GroupRange rg = rn;
             g = gn;
-            rn = g + 1 < gb ? group_range(d, g + 1) : GroupRange{0, 0};
+            const GroupRange rg = group_range(d, g);
             if (rg.start < base || rg.start - base != P || P > (1u << 30)) {
                 flush_pending(obuf, d, base, C, re, head, lane);
                 __syncwarp();
@@ -823,7 +824,6 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int ga, int
         }
         r = rnext;
         lo = lon;
-        prefetch_packed(pw, d, base, C, climit, lane);
     }
     flush_pending(obuf, d, base, C, re, head, lane);
     __syncwarp();
