@@ -644,7 +644,11 @@ __device__ __forceinline__ void load_round(RoundIn& in, const DevStream& d, long
 // round's merge steps use them.
 __device__ __forceinline__ void prefetch_packed(uint2 (&pw)[4], const DevStream& d, unsigned long long base,
                                                 uint32_t C, uint32_t climit, int lane) {
-    if (d.packed_vec) {
+    if (d.packed_vec && C + 128 <= climit) {  // all four chunks exist
+        const uint2* src = reinterpret_cast<const uint2*>(d.packed + (base >> 1)) + C + lane;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) pw[k] = __ldg(src + 32 * k);
+    } else if (d.packed_vec) {
         const uint2* src = reinterpret_cast<const uint2*>(d.packed + (base >> 1));
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -670,6 +674,17 @@ __device__ __forceinline__ void merge_steps(uint32_t* obuf, const DevStream& d, 
     uint2* ew2 = reinterpret_cast<uint2*>(obuf) + lane;
     uint4* ob = reinterpret_cast<uint4*>(d.out + base) + C + lane;
     const uint32_t c0 = C + lane;
+    if (d.out_vec && (C || head == 0) && steps <= 4) {  // the common case: no byte stores
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            if ((uint32_t)k < steps) {
+                const uint2 ew = ew2[32 * k];
+                ew2[32 * k] = make_uint2(0u, 0u);
+                ob[32 * k] = merge16(ew, pw[k]);
+            }
+        }
+        return;
+    }
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
         if ((uint32_t)k < steps) {
