@@ -550,7 +550,8 @@ def run_ours(args, rank, world, dev):
             "traffic": traffic,
             "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
             else "fallback 6.65 TB/s",
-            "kernel": "decode_kernel<128> (ecf8_decode_batch_flags launch, ECF8_DECODE_OVERLAP_PREVIOUS)",
+            "kernel": f"decode_kernel<{_lib.MAX_BATCH}> (ecf8_decode_batch_flags launch, "
+                      "ECF8_DECODE_OVERLAP_PREVIOUS)",
             "algorithmic_bytes_per_launch": int(per_launch_bytes),
             "mean_launch_us": round(mean_launch_ms * 1e3, 2),
         },

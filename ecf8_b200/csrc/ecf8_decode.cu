@@ -818,6 +818,16 @@ __device__ void decode_warp(Smem& S, WarpBuf& W, const DevStream& d, int ga, int
             ew2[lane] = t;
             C += 32 * steps;
         }
+        // Warm L2 with the packed words the next round's merge steps start
+        // from (chunks C .. C + 127): their register loads, issued after the
+        // next decode, then wait on L2 rather than DRAM.  A hint only; it
+        // holds no register or shared memory across the decode.
+        if (more && d.packed_vec) {
+            const uint2* src = reinterpret_cast<const uint2*>(d.packed + (base >> 1)) + C + lane;
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+                if (C + lane + 32 * k < climit) asm volatile("prefetch.global.L2 [%0];" ::"l"(src + 32 * k));
+        }
         __syncwarp();
         P = Pn;
         if (!more) break;

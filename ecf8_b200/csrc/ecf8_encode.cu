@@ -15,10 +15,13 @@
 //
 // Two launches per stream.  `plan` sums code lengths per 4096-element chunk
 // and scans the chunk sums (one CTA), so the host can size the outputs from
-// three numbers.  `emit` recomputes each element's absolute bit offset and
-// writes codes word by word: a thread owns 16 consecutive elements, writes the
-// 32-bit words wholly inside its bit range with plain stores and ORs the two
-// words it may share with its neighbours atomically.
+// three numbers.  `emit` recomputes each element's absolute bit offset; a
+// thread owns 16 consecutive elements and ORs their codes and the gap
+// nibbles of the windows they start into the chunk's stream words and gap
+// words, assembled in shared memory.  The CTA then stores the chunk's words
+// with coalesced plain stores, except the first and last stream and gap words,
+// which it may share with the neighbouring chunks: those it ORs atomically
+// into the zeroed outputs.
 
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -34,8 +37,14 @@ constexpr int kThreads = 256;
 constexpr int kPerThread = 16;
 constexpr int kChunk = kThreads * kPerThread;  // elements per chunk (4096)
 constexpr int kScanThreads = 1024;
+constexpr int kScanPer = 8;  // chunk sums per scan thread and pass
 constexpr long long kWindowBits = 8LL * ECF8_BYTES_PER_THREAD;          // 64
 constexpr long long kGroupBits = kWindowBits * ECF8_THREADS_PER_BLOCK;  // 32768
+constexpr int kMaxCodeBits = 16;
+// Stream words (from the chunk's first bit rounded down to 512) and gap words
+// (8 windows of 64 bits each) one chunk can touch.
+constexpr int kChunkWords = (kChunk * kMaxCodeBits + 511) / 32 + 1;
+constexpr int kChunkGapWords = kChunk * kMaxCodeBits / 512 + 1;
 
 struct CodeTable {
     uint32_t val[16];
@@ -46,82 +55,82 @@ struct CodeTable {
 
 thread_local int g_last_cuda_error = 0;
 
-__device__ __forceinline__ uint32_t block_sum(uint32_t v, uint32_t* red) {
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    uint32_t s = 0;
-    if (threadIdx.x < 32) {
-        s = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0u;
-        for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    }
-    return s;  // valid in thread 0
-}
-
-// Loads the 16 exponents of thread slot `i0` (clamped to n; absent = -1).
-__device__ __forceinline__ void load16(const uint8_t* ex, long long n, long long i0, int sym[kPerThread]) {
-    if (i0 + kPerThread <= n && ((reinterpret_cast<uintptr_t>(ex + i0) & 15) == 0)) {
-        const uint4 v = __ldg(reinterpret_cast<const uint4*>(ex + i0));
-        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int j = 0; j < kPerThread; ++j) sym[j] = (int)((w[j >> 2] >> (8 * (j & 3))) & 0xffu);
-    } else {
-#pragma unroll
-        for (int j = 0; j < kPerThread; ++j) sym[j] = (i0 + j < n) ? (int)__ldg(ex + i0 + j) : -1;
-    }
-}
-
 // The code table in shared memory: lanes look up different symbols, which
 // the kernel-parameter (constant) bank would serve one address at a time.
 struct SmemTable {
-    uint32_t val[16];
     uint32_t bits[16];
+    uint32_t code[16];  // code value << 16 | code length
 };
 
 __device__ __forceinline__ void load_table(SmemTable& t, const CodeTable& T) {
     if (threadIdx.x < 16) {
-        t.val[threadIdx.x] = T.val[threadIdx.x];
         t.bits[threadIdx.x] = T.bits[threadIdx.x];
+        t.code[threadIdx.x] = T.val[threadIdx.x] << 16 | T.bits[threadIdx.x];
     }
     __syncthreads();
 }
 
-__device__ __forceinline__ uint32_t sym_bits(const SmemTable& t, int s) {
-    return s < 0 ? 0u : t.bits[s & 15];
-}
-
-// Code bits of symbol s (bits 16..0) plus 1 << 17 for an exponent the code
-// table cannot encode: a byte above 15 or a symbol whose code length is 0.
-// Such exponents encode as nothing (their masked length is 0), so every
-// offset stays inside the planned stream; the plan counts them and emit
-// writes nothing when the count is not 0.
-__device__ __forceinline__ uint32_t sym_bits_and_invalid(const SmemTable& t, int s) {
-    if (s < 0) return 0u;
-    const uint32_t b = t.bits[s & 15];
-    return b | ((b == 0u || s > 15) ? (1u << 17) : 0u);
+// Code bits of exponent byte b (bits 16..0), or 1 << 17 for a byte the code
+// table cannot encode: one above 15 or a symbol whose code length is 0.  Such
+// exponents encode as nothing (their length counts 0), so every offset stays
+// inside the planned stream; the plan counts them and emit writes nothing
+// when the count is not 0.
+__device__ __forceinline__ void load_bits_table(uint32_t* lenx, const CodeTable& T) {
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) {
+        const uint32_t bits = b < 16 ? T.bits[b] : 0u;
+        lenx[b] = bits ? bits : (1u << 17);
+    }
+    __syncthreads();
 }
 
 constexpr int kInvalidShift = 32;  // chunk sums: code bits in the low half, invalid exponents in the high half
 
 // Per-chunk code-length sums (low half) and invalid-exponent counts (high half).
+// A CTA sums kSumChunks chunks, so each thread has that many 16-byte loads in
+// flight at once.  One reduction serves both sums: a chunk has at most
+// 4096 x 16 = 2^16 code bits (bits 16..0) and 4096 invalid exponents
+// (bits 29..17).
+constexpr int kSumChunks = 4;
+
 __global__ void __launch_bounds__(kThreads) chunk_bits_kernel(const uint8_t* __restrict__ ex, long long n,
                                                               const __grid_constant__ CodeTable T,
-                                                              unsigned long long* __restrict__ chunk) {
-    __shared__ uint32_t red[kThreads / 32];
-    __shared__ SmemTable t;
-    load_table(t, T);
-    const long long i0 = (long long)blockIdx.x * kChunk + (long long)threadIdx.x * kPerThread;
-    int sym[kPerThread];
-    load16(ex, n, i0, sym);
-    // One reduction for both sums: a chunk has at most 4096 x 16 = 2^16 code
-    // bits (bits 16..0) and 4096 invalid exponents (bits 29..17).
-    uint32_t v = 0;
+                                                              unsigned long long* __restrict__ chunk,
+                                                              long long n_chunks) {
+    __shared__ uint32_t red[kSumChunks][kThreads / 32];
+    __shared__ uint32_t lenx[256];
+    load_bits_table(lenx, T);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const long long c0 = (long long)blockIdx.x * kSumChunks;
+    uint4 raw[kSumChunks];
+    bool vec[kSumChunks];
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j) v += sym_bits_and_invalid(t, sym[j]);
-    v = block_sum(v, red);
-    if (threadIdx.x == 0)
-        chunk[blockIdx.x] = (unsigned long long)(v & 0x1ffffu) | ((unsigned long long)(v >> 17) << kInvalidShift);
+    for (int k = 0; k < kSumChunks; ++k) {
+        const long long i0 = (c0 + k) * kChunk + (long long)threadIdx.x * kPerThread;
+        vec[k] = i0 + kPerThread <= n && ((reinterpret_cast<uintptr_t>(ex + i0) & 15) == 0);
+        raw[k] = vec[k] ? __ldg(reinterpret_cast<const uint4*>(ex + i0)) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int k = 0; k < kSumChunks; ++k) {
+        const long long i0 = (c0 + k) * kChunk + (long long)threadIdx.x * kPerThread;
+        uint32_t v = 0;
+        if (vec[k]) {
+            const uint32_t w[4] = {raw[k].x, raw[k].y, raw[k].z, raw[k].w};
+#pragma unroll
+            for (int j = 0; j < kPerThread; ++j) v += lenx[__byte_perm(w[j >> 2], 0u, 0x4440u + (j & 3))];
+        } else {
+            for (int j = 0; j < kPerThread; ++j)
+                if (i0 + j < n) v += lenx[__ldg(ex + i0 + j)];
+        }
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) red[k][warp] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < kSumChunks && c0 + threadIdx.x < n_chunks) {
+        uint32_t v = 0;
+#pragma unroll
+        for (int w = 0; w < kThreads / 32; ++w) v += red[threadIdx.x][w];
+        chunk[c0 + threadIdx.x] = (unsigned long long)(v & 0x1ffffu) | ((unsigned long long)(v >> 17) << kInvalidShift);
+    }
 }
 
 // Exclusive scan of the chunk sums in place (chunk[c] becomes the first bit of
@@ -135,17 +144,33 @@ __global__ void __launch_bounds__(kScanThreads) scan_plan_kernel(const uint8_t* 
     __shared__ unsigned long long wsum[kScanThreads / 32];
     __shared__ unsigned long long carry;
     __shared__ unsigned long long invalid;
+    // One pass's chunk sums, then their exclusive offsets within the pass
+    // (at most 8192 x 2^16 = 2^29 bits): global memory is read and written
+    // with consecutive threads on consecutive chunks.
+    __shared__ __align__(16) uint32_t sv[kScanThreads * kScanPer];
     if (threadIdx.x == 0) carry = invalid = 0;
     __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    for (long long b = 0; b < n_chunks; b += kScanThreads) {
-        const long long i = b + threadIdx.x;
-        const unsigned long long raw = i < n_chunks ? chunk[i] : 0ull;
-        const unsigned long long x = raw & 0xffffffffull;
-        if (raw >> kInvalidShift) atomicAdd(&invalid, raw >> kInvalidShift);
-        unsigned long long v = x;
+    unsigned long long bad = 0;
+    for (long long b = 0; b < n_chunks; b += (long long)kScanThreads * kScanPer) {
+#pragma unroll
+        for (int k = 0; k < kScanPer; ++k) {
+            const long long i = b + k * kScanThreads + threadIdx.x;
+            const unsigned long long raw = i < n_chunks ? chunk[i] : 0ull;
+            sv[k * kScanThreads + threadIdx.x] = (uint32_t)raw;  // at most 2^16 code bits per chunk
+            bad += raw >> kInvalidShift;
+        }
+        __syncthreads();
+        // Thread t scans chunks b + 8t .. b + 8t + 7.
+        uint4* mine = reinterpret_cast<uint4*>(sv + threadIdx.x * kScanPer);
+        const uint4 p0 = mine[0], p1 = mine[1];
+        const uint32_t xs[kScanPer] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        uint32_t x = 0;
+#pragma unroll
+        for (int k = 0; k < kScanPer; ++k) x += xs[k];
+        uint32_t v = x;
         for (int o = 1; o < 32; o <<= 1) {
-            const unsigned long long y = __shfl_up_sync(0xffffffffu, v, o);
+            const uint32_t y = __shfl_up_sync(0xffffffffu, v, o);
             if (lane >= o) v += y;
         }
         if (lane == 31) wsum[warp] = v;
@@ -160,12 +185,26 @@ __global__ void __launch_bounds__(kScanThreads) scan_plan_kernel(const uint8_t* 
         }
         __syncthreads();
         const unsigned long long c0 = carry;
-        const unsigned long long incl = v + (warp ? wsum[warp - 1] : 0ull);
-        if (i < n_chunks) chunk[i] = c0 + incl - x;
+        const uint32_t incl = v + (warp ? (uint32_t)wsum[warp - 1] : 0u);
+        uint32_t run = incl - x, o[kScanPer];
+#pragma unroll
+        for (int k = 0; k < kScanPer; ++k) {
+            o[k] = run;
+            run += xs[k];
+        }
+        mine[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        mine[1] = make_uint4(o[4], o[5], o[6], o[7]);
         __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kScanPer; ++k) {
+            const long long i = b + k * kScanThreads + threadIdx.x;
+            if (i < n_chunks) chunk[i] = c0 + sv[k * kScanThreads + threadIdx.x];
+        }
         if (threadIdx.x == kScanThreads - 1) carry = c0 + incl;
         __syncthreads();
     }
+    if (bad) atomicAdd(&invalid, bad);
+    __syncthreads();
     if (threadIdx.x == 0) {
         const unsigned long long total = carry;
         chunk[n_chunks] = total;
@@ -185,24 +224,99 @@ __global__ void __launch_bounds__(kScanThreads) scan_plan_kernel(const uint8_t* 
 
 __device__ __forceinline__ uint32_t bswap32(uint32_t x) { return __byte_perm(x, 0, 0x0123); }
 
-// ORs `v` (big-endian bit order) into stream word `w`.  Words are byte
-// swapped into memory order.
-__device__ __forceinline__ void put_word(uint32_t* enc32, long long w, uint32_t v, bool shared_word) {
-    if (!v) return;
-    if (shared_word)
-        atomicOr(enc32 + w, bswap32(v));
-    else
-        enc32[w] = bswap32(v);
-}
-
-__device__ __forceinline__ void put_gap(uint32_t* gaps32, unsigned long long window, uint32_t gap) {
-    // Window j's 4 bits sit in byte j/2, high nibble for even j (np.packbits order).
-    const unsigned long long byte = window >> 1;
+// Window j's 4 bits sit in byte j/2, high nibble for even j (np.packbits
+// order); gap word j/8 holds bytes 4(j/8) .. 4(j/8)+3.  `q` is a code's
+// start bit relative to a 512-bit-aligned origin, `gw` its gap word there.
+__device__ __forceinline__ void put_gap(uint32_t* sg, uint32_t gw, uint32_t q) {
+    const uint32_t window = q >> 6;  // parity and byte-in-word as for the absolute window
+    const uint32_t gap = q & 63u;
     const uint32_t nib = (window & 1) ? gap : (gap << 4);
-    if (nib) atomicOr(gaps32 + (byte >> 2), nib << (8 * (byte & 3)));
+    if (nib) atomicOr(sg + gw, nib << (8 * ((window >> 1) & 3)));
 }
 
-__global__ void __launch_bounds__(kThreads) emit_kernel(const uint8_t* __restrict__ ex, long long n,
+// Stores words [0, count) of a chunk's shared-memory buffer at dst + first;
+// the first and last word with atomicOr (the neighbouring chunks may own bits
+// of them), the rest with plain stores.
+__device__ __forceinline__ void store_chunk_words(uint32_t* dst, unsigned long long first, const uint32_t* src,
+                                                  int count, bool swap) {
+    for (int k = threadIdx.x; k < count; k += blockDim.x) {
+        const uint32_t v = swap ? bswap32(src[k]) : src[k];
+        if (k == 0 || k == count - 1) {
+            if (v) atomicOr(dst + first + k, v);
+        } else {
+            dst[first + k] = v;
+        }
+    }
+}
+
+// Emits one thread's codes (its elements i0 .. i0 + 15 below n, the first
+// starting at stream bit b0) into the chunk's shared stream words `sw` (word
+// 0 = stream word A / 32) and gap words `sg` (word 0 = gap word A / 512).
+// Positions are 32-bit: q = bit - (A - Ag), measured from the start of the
+// 32768-bit group holding A (A is 512-aligned, Ag = A mod 32768), so one XOR
+// of consecutive code starts tells a new window (>= 64) and a new group
+// (>= 32768) (utils.py:392-406).  Codes shift into a 64-bit accumulator; each
+// time one completes a 32-bit word, that word is ORed into `sw` (the first
+// and last may hold the neighbouring threads' bits).  Output positions go
+// straight to `op`: each is written by the one thread whose code starts its
+// group.
+__device__ __forceinline__ void emit_thread(uint32_t* sw, uint32_t* sg, unsigned long long A, uint32_t Ag,
+                                            const SmemTable& t, const CodeTable& T, uint64_t* __restrict__ op,
+                                            long long n, long long i0, const uint8_t* __restrict__ ex,
+                                            const uint32_t (&w)[4], unsigned long long b0,
+                                            unsigned long long total) {
+    uint32_t q = (uint32_t)(b0 - A) + Ag;
+    // Start of the element before this thread's first one; for element 0 of
+    // the stream a value that differs from q in every bit (window 0 and
+    // group 0 begin there).
+    uint32_t prev = (i0 == 0) ? ~q : q - T.bits[__ldg(ex + i0 - 1) & 15];
+    const uint32_t wofs = Ag >> 5, gofs = Ag >> 9;
+    const unsigned long long group0 = A >> 15;
+    uint32_t lo = 0, hi = 0;  // accumulator: the low (q mod 32) bits are the open word's
+    const int m = (int)min((long long)kPerThread, n - i0);
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j) {
+        if (j >= m) break;
+        const uint32_t e = t.code[(w[j >> 2] >> (8 * (j & 3))) & 15u];
+        const uint32_t len = e & 31u;
+        const uint32_t x = q ^ prev;
+        if (x >= 64u) {
+            put_gap(sg, (q >> 9) - gofs, q);
+            if (x >= 32768u) op[group0 + (q >> 15)] = (uint64_t)(i0 + j);
+        }
+        hi = __funnelshift_l(lo, hi, len);
+        lo = (lo << len) | (e >> 16);
+        const uint32_t end = q + len;
+        if ((end ^ q) >= 32u) atomicOr(sw + (q >> 5) - wofs, __funnelshift_r(lo, hi, end));
+        prev = q;
+        q = end;
+    }
+    if (i0 + m == n && (total % 8)) {
+        // utils.py:439-459: the last thread completes the final byte with the
+        // EOF code's leading bits, and adds the gap / output position of the
+        // end if it starts a new window / group.
+        const uint32_t r = (uint32_t)(total % 8);
+        const uint32_t room = 8 - r;
+        const uint32_t ebits = (uint32_t)T.eof_bits;
+        const uint32_t tail = (r + ebits >= 8) ? (T.eof_val >> (ebits - room)) & ((1u << room) - 1u)
+                                               : (T.eof_val << (room - ebits)) & ((1u << room) - 1u);
+        const uint32_t x = q ^ prev;
+        if (x >= 64u) {
+            put_gap(sg, (q >> 9) - gofs, q);
+            if (x >= 32768u) op[group0 + (q >> 15)] = (uint64_t)n;
+        }
+        hi = __funnelshift_l(lo, hi, room);
+        lo = (lo << room) | tail;
+        const uint32_t end = q + room;
+        if ((end ^ q) >= 32u) atomicOr(sw + (q >> 5) - wofs, __funnelshift_r(lo, hi, end));
+        q = end;
+    }
+    if (q & 31u) atomicOr(sw + (q >> 5) - wofs, lo << (32 - (q & 31u)));
+}
+
+// Eight CTAs per SM (32 registers a thread): the CTAs' global loads and
+// barriers overlap one another's emit work.
+__global__ void __launch_bounds__(kThreads, 8) emit_kernel(const uint8_t* __restrict__ ex, long long n,
                                                         const __grid_constant__ CodeTable T,
                                                         const unsigned long long* __restrict__ chunk,
                                                         uint8_t* __restrict__ encoded, long long n_bytes,
@@ -210,14 +324,35 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(const uint8_t* __restric
                                                         uint64_t* __restrict__ op) {
     __shared__ uint32_t wsum[kThreads / 32];
     __shared__ SmemTable t;
-    load_table(t, T);
+    __shared__ uint32_t sw[kChunkWords];
+    __shared__ uint32_t sg[kChunkGapWords];
     const long long c = blockIdx.x;
+    const unsigned long long total = __ldg(chunk + gridDim.x), bad = __ldg(chunk + gridDim.x + 1);
+    const unsigned long long cb0 = __ldg(chunk + c), cb1 = __ldg(chunk + c + 1);
+    for (int k = threadIdx.x; k < kChunkWords; k += kThreads) sw[k] = 0u;
+    for (int k = threadIdx.x; k < kChunkGapWords; k += kThreads) sg[k] = 0u;
+    load_table(t, T);  // ends with a barrier
     const long long i0 = c * kChunk + (long long)threadIdx.x * kPerThread;
-    int sym[kPerThread];
-    load16(ex, n, i0, sym);
+    uint32_t w[4];
+    if (i0 + kPerThread <= n && ((reinterpret_cast<uintptr_t>(ex + i0) & 15) == 0)) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(ex + i0));
+        w[0] = v.x;
+        w[1] = v.y;
+        w[2] = v.z;
+        w[3] = v.w;
+    } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            uint32_t v = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) v |= (i0 + 4 * k + j < n ? (uint32_t)__ldg(ex + i0 + 4 * k + j) : 0u) << (8 * j);
+            w[k] = v;
+        }
+    }
     uint32_t local = 0;
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j) local += sym_bits(t, sym[j]);
+    for (int j = 0; j < kPerThread; ++j)
+        local += (i0 + j < n) ? t.bits[(w[j >> 2] >> (8 * (j & 3))) & 15u] : 0u;
     // block exclusive scan of per-thread bit counts
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t v = local;
@@ -236,80 +371,22 @@ __global__ void __launch_bounds__(kThreads) emit_kernel(const uint8_t* __restric
         if (lane < kThreads / 32) wsum[lane] = s;
     }
     __syncthreads();
-    const unsigned long long total = chunk[gridDim.x];
-    if (chunk[gridDim.x + 1]) return;  // the plan counted invalid exponents: no stream
-    const unsigned long long b0 = chunk[c] + (v - local) + (warp ? wsum[warp - 1] : 0u);
-    if (local == 0) return;
-
-    // Start bit of the element before this thread's first one.
-    unsigned long long prev_start;
-    if (i0 == 0)
-        prev_start = ~0ull;
-    else
-        prev_start = b0 - T.bits[__ldg(ex + i0 - 1) & 15];
-
-    uint32_t* enc32 = reinterpret_cast<uint32_t*>(encoded);
-    const long long first_word = (long long)(b0 >> 5);
-    unsigned long long pos = b0;
-    long long cur_w = first_word;
-    uint32_t cur = 0;
-    long long last_i = -1;
-    unsigned long long last_start = 0;
-#pragma unroll
-    for (int j = 0; j < kPerThread; ++j) {
-        if (sym[j] < 0) break;
-        const uint32_t len = t.bits[sym[j] & 15];
-        const uint32_t code = t.val[sym[j] & 15];
-        const long long i = i0 + j;
-        // window / group bookkeeping (utils.py:392-406)
-        const unsigned long long ps = (j == 0) ? prev_start : last_start;
-        if (i == 0 || (ps >> 6) != (pos >> 6)) put_gap(gaps32, pos >> 6, (uint32_t)(pos & 63));
-        if (i == 0 || (ps / kGroupBits) != (pos / kGroupBits)) op[pos / kGroupBits] = (uint64_t)i;
-        // place the code's bits [pos, pos + len) -- len <= 16, so at most two words
-        const uint32_t off = (uint32_t)(pos & 31);
-        const long long w = (long long)(pos >> 5);
-        if (w != cur_w) {
-            put_word(enc32, cur_w, cur, cur_w == first_word);
-            cur_w = w;
-            cur = 0;
-        }
-        if (off + len <= 32) {
-            cur |= code << (32 - off - len);
-        } else {
-            const uint32_t spill = off + len - 32;
-            cur |= code >> spill;
-            put_word(enc32, cur_w, cur, cur_w == first_word);
-            cur_w = w + 1;
-            cur = code << (32 - spill);
-        }
-        last_start = pos;
-        last_i = i;
-        pos += len;
+    if (bad) return;  // the plan counted invalid exponents: no stream (uniform)
+    const unsigned long long b0 = cb0 + (v - local) + (warp ? wsum[warp - 1] : 0u);
+    // The chunk's codes start in bits [cb0, cb1); with the EOF completion of
+    // the last byte (bits from `total`, in the word and gap word of bit
+    // total - 1) they touch stream words [cb0/32, (cb1-1)/32] and gap words
+    // [cb0/512, (cb1-1)/512].  The shared buffers start at A = cb0 rounded
+    // down to 512 bits.
+    const unsigned long long A = cb0 & ~511ull;
+    if (local) emit_thread(sw, sg, A, (uint32_t)(A & 32767u), t, T, op, n, i0, ex, w, b0, total);
+    __syncthreads();
+    if (cb1 > cb0) {
+        const unsigned long long w0 = cb0 >> 5;
+        store_chunk_words(reinterpret_cast<uint32_t*>(encoded), w0, sw + (w0 - (A >> 5)),
+                          (int)(((cb1 - 1) >> 5) - w0 + 1), true);
+        store_chunk_words(gaps32, cb0 >> 9, sg, (int)(((cb1 - 1) >> 9) - (cb0 >> 9) + 1), false);
     }
-    // The last word may be shared with the next thread.
-    const bool is_last_thread = (last_i == n - 1);
-    if (is_last_thread && (total % 8)) {
-        // utils.py:439-459: complete the final byte with the EOF code's
-        // leading bits, add the gap / output position of the end if it starts
-        // a new window / group.
-        const uint32_t r = (uint32_t)(total % 8);
-        const uint32_t room = 8 - r;
-        const uint32_t ebits = (uint32_t)T.eof_bits;
-        const uint32_t tail = (r + ebits >= 8) ? (T.eof_val >> (ebits - room)) & ((1u << room) - 1u)
-                                               : (T.eof_val << (room - ebits)) & ((1u << room) - 1u);
-        const long long w = (long long)(total >> 5);
-        const uint32_t boff = (uint32_t)(total & 31);  // first free bit in word w
-        const uint32_t shifted = tail << (32 - boff - room);
-        if (w != cur_w) {
-            put_word(enc32, cur_w, cur, true);
-            cur_w = w;
-            cur = 0;
-        }
-        cur |= shifted;
-        if ((last_start >> 6) != (total >> 6)) put_gap(gaps32, total >> 6, (uint32_t)(total & 63));
-        if ((last_start / kGroupBits) != (total / kGroupBits)) op[total / kGroupBits] = (uint64_t)n;
-    }
-    put_word(enc32, cur_w, cur, true);
     (void)n_bytes;
 }
 
@@ -383,7 +460,9 @@ int ecf8_encode_plan(const uint8_t* exponents, int64_t n, const uint8_t* code_bi
     unsigned long long* chunk = reinterpret_cast<unsigned long long*>(workspace);
     unsigned long long* plan = chunk + chunks + 2;
     if (chunks > 0x7fffffffLL) return ECF8_ERR_INVALID_ARGUMENT;
-    if (chunks > 0) chunk_bits_kernel<<<(unsigned)chunks, kThreads, 0, s>>>(exponents, n, T, chunk);
+    if (chunks > 0)
+        chunk_bits_kernel<<<(unsigned)((chunks + kSumChunks - 1) / kSumChunks), kThreads, 0, s>>>(exponents, n, T,
+                                                                                             chunk, chunks);
     scan_plan_kernel<<<1, kScanThreads, 0, s>>>(exponents, n, T, chunk, chunks, plan);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_fail(e);
@@ -485,7 +564,9 @@ int ecf8_encode_noalloc(const uint8_t* exponents, int64_t n, const uint8_t* code
     if (e == cudaSuccess && gaps_capacity > 0) e = cudaMemsetAsync(gaps, 0, (size_t)gaps_capacity, s);
     if (e == cudaSuccess) e = cudaMemsetAsync(output_positions, 0, (size_t)output_positions_capacity * 8, s);
     if (e != cudaSuccess) return cuda_fail(e);
-    if (chunks > 0) chunk_bits_kernel<<<(unsigned)chunks, kThreads, 0, s>>>(exponents, n, T, chunk);
+    if (chunks > 0)
+        chunk_bits_kernel<<<(unsigned)((chunks + kSumChunks - 1) / kSumChunks), kThreads, 0, s>>>(exponents, n, T,
+                                                                                             chunk, chunks);
     scan_plan_kernel<<<1, kScanThreads, 0, s>>>(exponents, n, T, chunk, chunks, plan);
     if (chunks > 0)
         emit_kernel<<<(unsigned)chunks, kThreads, 0, s>>>(exponents, n, T, chunk, encoded, 0,
