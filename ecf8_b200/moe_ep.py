@@ -150,13 +150,24 @@ class SparseMoE(nn.Module):
             recv_e = _all_to_all(send_e, sc, rc, self.group)
         else:
             recv_x, recv_e = send_x, send_e
-        out = torch.empty_like(recv_x)
-        used = recv_e.unique().tolist()
+        # Received assignments grouped by local expert (stable: each expert's
+        # rows stay in arrival order), so each expert runs on one contiguous
+        # slice; one host read of the per-expert counts per layer.
+        first = self.rank * self.per
+        by_e = torch.argsort(recv_e, stable=True)
+        counts = torch.bincount(recv_e - first, minlength=self.per).tolist()
+        used = [first + i for i, c in enumerate(counts) if c]
         if self.expert_loader is not None:
             self.expert_loader(used)
-        for e in used:
-            idx = (recv_e == e).nonzero().squeeze(1)
-            out[idx] = self.experts[str(e)](recv_x[idx])
+        xs_e = recv_x[by_e]
+        ys_e = torch.empty_like(xs_e)
+        off = 0
+        for i, c in enumerate(counts):
+            if c:
+                ys_e[off:off + c] = self.experts[str(first + i)](xs_e[off:off + c])
+                off += c
+        out = torch.empty_like(recv_x)
+        out[by_e] = ys_e
         back = _all_to_all(out, rc, sc, self.group) if self.world > 1 else out
         per_assign = torch.empty_like(back)
         per_assign[order] = back
@@ -254,29 +265,42 @@ _EXPERT_PARTS = ("down_proj", "gate_proj", "up_proj")  # sorted names: the strea
 class ExpertStreamLoader:
     """The compressed experts of one MoE layer on this rank: each expert's
     gate/up/down weights are one ECF8 stream (with its prepared decode
-    table); a call decodes the given experts with one batched launch into a
-    per-layer scratch and points the experts' Linear weights at it."""
+    table).  Every owned expert has a fixed slot in `scratch` (slot i for the
+    rank's i-th expert; all layers share the slots, as they run one after
+    another), so its Linear weights point at the slot once, here, and its
+    launch descriptor is checked and built once.  A call decodes the given
+    experts into their slots with one batched launch on the current stream."""
 
     def __init__(self, moe, streams, scratch):
+        from .run import _check_stream, _stream_struct
         self.moe = moe
-        self.streams = streams  # global expert index -> stream dict
+        self.streams = streams  # global expert index -> stream dict (kept alive for the descriptors)
+        self.scratch = scratch
+        first = moe.rank * moe.per
         self.per = next(iter(streams.values()))["packed_other_4bits"].numel() * 2
-        self.scratch = scratch  # shared by all layers: they run one after another
-
-    def __call__(self, used):
-        from .run import decode_streams
-        if not used:
-            return
-        outs = [self.scratch[i * self.per:(i + 1) * self.per] for i in range(len(used))]
-        decode_streams([self.streams[e] for e in used], outs)
-        for e, flat in zip(used, outs):
-            expert = self.moe.experts[str(e)]
+        self.desc = {}
+        for e, st in streams.items():
+            flat = scratch[(e - first) * self.per:(e - first + 1) * self.per]
+            table = st.get("decode_table")
+            _check_stream(st, flat, scratch.device, table)
+            self.desc[e] = _stream_struct(st, flat, table)
+            expert = moe.experts[str(e)]
             off = 0
             for part in _EXPERT_PARTS:
                 lin = getattr(expert, part)
                 n = lin.out_features * lin.in_features
                 lin.weight = flat[off:off + n].view(lin.out_features, lin.in_features)
                 off += n
+
+    def __call__(self, used):
+        from . import _lib
+        if not used:
+            return
+        arr = (_lib.Ecf8Stream * len(used))(*[self.desc[e] for e in used])
+        cs = torch.cuda.current_stream(self.scratch.device)
+        st = _lib.lib().ecf8_decode_batch_flags(arr, len(used), _lib.THREADS_PER_BLOCK, _lib.BYTES_PER_THREAD, 0,
+                                                cs.cuda_stream)
+        _lib.check(st, "ecf8_decode_batch_flags")
 
 
 def _flat_fp8(modules):
