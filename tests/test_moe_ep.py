@@ -1,6 +1,7 @@
 """Expert-parallel MoE generation on CPU: two gloo ranks (experts split
 4 + 4, tokens exchanged with all-to-all) generate what one process holding
-all experts generates for both ranks' prompts."""
+all experts generates for both ranks' prompts: the same tokens and the same
+per-step logit sums, bit for bit."""
 import os
 import subprocess
 import sys
@@ -37,4 +38,7 @@ def test_two_rank_expert_parallel_matches_one_process(tmp_path):
     got = torch.load(out)
     tokens, sums = _single_process_reference(2, 2, 8, 4)
     assert torch.equal(got["tokens"], tokens)
-    torch.testing.assert_close(got["logit_sums"], sums, rtol=1e-3, atol=1e-3)
+    # Bit for bit: every expert runs on the same rows in the same order in
+    # both set-ups (assignments grouped by expert, stable, source rank
+    # major), and the combine sums each token's outputs in a fixed order.
+    assert torch.equal(got["logit_sums"], sums)
