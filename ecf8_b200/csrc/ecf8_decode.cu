@@ -30,7 +30,9 @@
 //    of look-ahead per lane) and gap byte are loaded into registers while the
 //    previous round is placed and merged; the packed sign+mantissa nibbles a
 //    round's merge needs are loaded right after its decode, so they are not
-//    live (holding registers) during the decode loop.
+//    live (holding registers) during the decode loop, and the round before
+//    warms L2 with them (prefetch.global.L2), so those loads wait on L2
+//    rather than DRAM.
 //  * Merge in whole-warp steps.  Once the nibble buffer holds 512 elements
 //    past the merge cursor, each lane merges one 16-element chunk per step
 //    (byte-permute/logic ops) and writes it with one 16-byte store; what is
