@@ -18,13 +18,23 @@ ERR_CUDA = 3
 ERR_TOO_LARGE = 4
 NOALLOC_MAX_ELEMENTS = 268435456
 
-ABI_VERSION = 7
+ABI_VERSION = 8
 TABLE_BYTES = 86544  # prepared decode table (ecf8_build_table)
 MAX_LUTS = 18
 MAX_BATCH = 256
 DECODE_OVERLAP_PREVIOUS = 1  # ecf8_decode_batch_flags: may start while the stream's previous kernel runs
+DECODE_CTAS_SHIFT = 16  # ecf8_decode_batch_flags bits 31..16: at most this many CTAs (0: one per SM)
+
 THREADS_PER_BLOCK = 512
 BYTES_PER_THREAD = 8
+
+
+def decode_ctas(n):
+    """ecf8_decode_batch_flags bits for a launch of at most n CTAs (1..65535)."""
+    if not 1 <= n <= 0xFFFF:
+        raise ValueError("the CTA limit is 1..65535")
+    return n << DECODE_CTAS_SHIFT
+
 
 _c_u8p = ctypes.c_void_p
 _i64 = ctypes.c_int64

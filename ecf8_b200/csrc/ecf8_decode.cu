@@ -1015,8 +1015,9 @@ int check_format(int threads_per_block, int bytes_per_thread) {
     return ECF8_OK;
 }
 
+// max_ctas: at most this many CTAs (0: one per SM, the resident limit).
 template <int MAXS>
-int launch(const ecf8_stream* streams, int n, cudaStream_t stream, bool overlap) {
+int launch(const ecf8_stream* streams, int n, cudaStream_t stream, bool overlap, int max_ctas) {
     Batch<MAXS> B;
     long long total = 0;
     int m = 0;
@@ -1038,6 +1039,7 @@ int launch(const ecf8_stream* streams, int n, cudaStream_t stream, bool overlap)
     int st = device_info(&info);
     if (st != ECF8_OK) return st;
     long long grid = (long long)info.sms * info.blocks_per_sm;
+    if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
     if (grid > total) grid = total;
     if (!overlap) {
         decode_kernel<MAXS><<<(unsigned)grid, kThreads, sizeof(Smem), stream>>>(B);
@@ -1063,7 +1065,7 @@ int launch(const ecf8_stream* streams, int n, cudaStream_t stream, bool overlap)
 }
 
 int decode_batch(const ecf8_stream* streams, int n_streams, int threads_per_block, int bytes_per_thread,
-                 bool overlap, void* cuda_stream) {
+                 bool overlap, int max_ctas, void* cuda_stream) {
     int st = check_format(threads_per_block, bytes_per_thread);
     if (st != ECF8_OK) return st;
     if (n_streams < 0 || (n_streams > 0 && !streams)) return ECF8_ERR_INVALID_ARGUMENT;
@@ -1075,7 +1077,7 @@ int decode_batch(const ecf8_stream* streams, int n_streams, int threads_per_bloc
     }
     for (int i = 0; i < n_streams; i += ECF8_MAX_BATCH) {
         const int n = n_streams - i < ECF8_MAX_BATCH ? n_streams - i : ECF8_MAX_BATCH;
-        st = launch<ECF8_MAX_BATCH>(streams + i, n, (cudaStream_t)cuda_stream, overlap);
+        st = launch<ECF8_MAX_BATCH>(streams + i, n, (cudaStream_t)cuda_stream, overlap, max_ctas);
         if (st != ECF8_OK) return st;
     }
     return ECF8_OK;
@@ -1106,19 +1108,21 @@ int ecf8_decode(const uint8_t* luts, const uint8_t* encoded, const uint8_t* pack
     s.outputs = outputs;
     s.n_elements = n_elements;
     s.table = nullptr;
-    return ecf8::launch<1>(&s, 1, (cudaStream_t)cuda_stream, false);
+    return ecf8::launch<1>(&s, 1, (cudaStream_t)cuda_stream, false, 0);
 }
 
 int ecf8_decode_batch(const ecf8_stream* streams, int n_streams, int threads_per_block,
                       int bytes_per_thread, void* cuda_stream) {
-    return ecf8::decode_batch(streams, n_streams, threads_per_block, bytes_per_thread, false, cuda_stream);
+    return ecf8::decode_batch(streams, n_streams, threads_per_block, bytes_per_thread, false, 0, cuda_stream);
 }
 
 int ecf8_decode_batch_flags(const ecf8_stream* streams, int n_streams, int threads_per_block,
                             int bytes_per_thread, uint32_t flags, void* cuda_stream) {
-    if (flags & ~(uint32_t)ECF8_DECODE_OVERLAP_PREVIOUS) return ECF8_ERR_INVALID_ARGUMENT;
+    if (flags & ~((uint32_t)ECF8_DECODE_OVERLAP_PREVIOUS | ECF8_DECODE_CTAS(0xffffu)))
+        return ECF8_ERR_INVALID_ARGUMENT;
+    const int max_ctas = (int)(flags >> ECF8_DECODE_CTAS_SHIFT);
     return ecf8::decode_batch(streams, n_streams, threads_per_block, bytes_per_thread,
-                              (flags & ECF8_DECODE_OVERLAP_PREVIOUS) != 0, cuda_stream);
+                              (flags & ECF8_DECODE_OVERLAP_PREVIOUS) != 0, max_ctas, cuda_stream);
 }
 
 int ecf8_build_table(const uint8_t* luts, int n_luts, uint32_t* table, void* cuda_stream) {

@@ -129,6 +129,8 @@ def main(argv=None):
     ap.add_argument("--warm_tokens", type=int, default=None, help="warm-up generation length (default: num_tokens)")
     ap.add_argument("--prefetch", action="store_true",
                     help="compressed arm: decode each layer one layer ahead on a side stream")
+    ap.add_argument("--prefetch_ctas", type=int, default=0,
+                    help="with --prefetch: CTAs of each side-stream decode (0: one per SM)")
     ap.add_argument("--fp8_matmul", choices=["auto", "dequant"], default="auto",
                     help="auto: block-scaled FP8 GEMM on e4m3 weights; dequant: bf16 expansion + bf16 matmul")
     args = ap.parse_args(argv)
@@ -162,8 +164,10 @@ def main(argv=None):
         compress_model_in_place(model)
         if args.prefetch:
             from .run import enable_decode_prefetch
-            enable_decode_prefetch(model)
+            enable_decode_prefetch(model, ctas=args.prefetch_ctas)
         line["decode_prefetch"] = bool(args.prefetch)
+        if args.prefetch:
+            line["decode_prefetch_ctas"] = args.prefetch_ctas
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
         TensorManager.clear_device()

@@ -130,7 +130,8 @@ def _check_stream(s, out, device, table=None):
 
 
 def decode_stream(luts, encoded, packed_other_4bits, output_positions, gaps, out=None,
-                  threads_per_block=512, bytes_per_thread=8, stream=None, table=None, overlap_previous=False):
+                  threads_per_block=512, bytes_per_thread=8, stream=None, table=None, overlap_previous=False,
+                  max_ctas=0):
     """Decodes one ECF8 stream (the five buffers a compressed block holds) into
     `out` (e4m3 or uint8, n = 2 * packed_other_4bits.numel() elements;
     allocated if None).  `table` is the stream's prepared decode table
@@ -139,8 +140,10 @@ def decode_stream(luts, encoded, packed_other_4bits, output_positions, gaps, out
     device).  With overlap_previous=True the launch may start while the
     stream's previous kernel runs and writes `out` only after it has finished
     (ECF8_DECODE_OVERLAP_PREVIOUS); the caller guarantees that no work still
-    in flight on the stream writes the stream buffers or the table.  Returns
-    `out`."""
+    in flight on the stream writes the stream buffers or the table.  With
+    max_ctas > 0 the launch uses at most that many CTAs (ECF8_DECODE_CTAS)
+    instead of one per SM, leaving the other SMs to kernels on other streams.
+    Returns `out`."""
     device = encoded.device
     if device.type != "cuda":
         raise ValueError("ECF8 decode runs on a CUDA device; move the stream buffers there first")
@@ -153,10 +156,11 @@ def decode_stream(luts, encoded, packed_other_4bits, output_positions, gaps, out
     L = _lib.lib()
     with torch.cuda.device(device):
         cs = stream if stream is not None else torch.cuda.current_stream(device)
-        if overlap_previous:
+        if overlap_previous or max_ctas:
+            flags = (_lib.DECODE_OVERLAP_PREVIOUS if overlap_previous else 0) | \
+                (_lib.decode_ctas(max_ctas) if max_ctas else 0)
             arr = (_lib.Ecf8Stream * 1)(_stream_struct(s, out, table))
-            st = L.ecf8_decode_batch_flags(arr, 1, threads_per_block, bytes_per_thread,
-                                           _lib.DECODE_OVERLAP_PREVIOUS, cs.cuda_stream)
+            st = L.ecf8_decode_batch_flags(arr, 1, threads_per_block, bytes_per_thread, flags, cs.cuda_stream)
         elif table is None:
             st = L.ecf8_decode(luts.data_ptr(), encoded.data_ptr(), packed_other_4bits.data_ptr(),
                                output_positions.data_ptr(), gaps.data_ptr(), out.data_ptr(),
@@ -316,13 +320,19 @@ class _Prefetch:
     """Per-device state of the prefetching hook: a side stream, two scratch
     buffers (each the size of the largest block, allocated once, so no buffer
     is freed while a side-stream decode writes it) used in turn by
-    consecutive blocks, and the decodes in flight."""
+    consecutive blocks, the decodes in flight (block -> buffer index) and the
+    events that order the two streams: per buffer, one recorded after the
+    side-stream decode into it; one recorded on the compute stream before
+    each side-stream decode.  An event is re-recorded only after every wait
+    on its previous record has been enqueued."""
 
     def __init__(self, device, n_max):
         self.device = device
         self.side = torch.cuda.Stream(device)
         self.bufs = [torch.empty(n_max, dtype=torch.float8_e4m3fn, device=device) for _ in range(2)]
-        self.pending = {}  # module -> (buffer index, event after its decode)
+        self.pending = {}
+        self.ready = [torch.cuda.Event(), torch.cuda.Event()]
+        self.done = torch.cuda.Event()
 
     def buffer(self, i, n):
         return self.bufs[i][:n]
@@ -379,6 +389,24 @@ def get_hook(threads_per_block, bytes_per_thread):
     return decode_hook
 
 
+def _prefetch_launch(st, nxt, slot, tpb, bpt, ctas):
+    """Side-stream decode of block `nxt` into buffer `slot`, from a launch
+    descriptor checked and built once per (block, buffer)."""
+    n = _n_elements(nxt)
+    buf = st.buffer(slot, n)
+    table = nxt.ecf8_decode_table
+    key = (buf.data_ptr(), table.data_ptr()) + tuple(nxt._buffers[k].data_ptr() for k in STREAM_BUFFERS)
+    kept = nxt.__dict__.setdefault("_ecf8_pf_launch", {})
+    ent = kept.get(slot)
+    if ent is None or ent[0] != key:
+        s = {k: nxt._buffers[k] for k in STREAM_BUFFERS}
+        _check_stream(s, buf, st.device, table)
+        ent = kept[slot] = (key, (_lib.Ecf8Stream * 1)(_stream_struct(s, buf, table)))
+    rc = _lib.lib().ecf8_decode_batch_flags(ent[1], 1, tpb, bpt, _lib.decode_ctas(ctas) if ctas else 0,
+                                            st.side.cuda_stream)
+    _lib.check(rc, "ecf8_decode_batch_flags")
+
+
 def _prefetch_hook(module, nxt, tpb, bpt):
     device = module.encoded.device
     st = _PREFETCH.get(device)
@@ -386,41 +414,37 @@ def _prefetch_hook(module, nxt, tpb, bpt):
         n_max = max([_n_elements(m) for m in _prefetch_blocks(module)] + [_n_elements(module), _n_elements(nxt)])
         st = _PREFETCH[device] = _Prefetch(device, n_max)
     cur = torch.cuda.current_stream(device)
-    if module in st.pending:  # decoded ahead: wait for that decode on this stream
-        slot, ready = st.pending.pop(module)
-        cur.wait_event(ready)
-        buf = st.buffer(slot, _n_elements(module))
+    slot = st.pending.pop(module, None)
+    if slot is not None:  # decoded ahead: wait for that decode on this stream
+        cur.wait_event(st.ready[slot])
     else:  # not decoded ahead (first block of a forward, or another order): decode here,
         # after every side-stream decode still writing either buffer
         cur.wait_stream(st.side)
-        used = {s for s, _ in st.pending.values()}
-        slot = 0 if 0 not in used else 1
-        st.pending = {m: v for m, v in st.pending.items() if v[0] != slot}
-        buf = st.buffer(slot, _n_elements(module))
-        _decode_block(module, buf, tpb, bpt)
-    inject_weights(module, buf)
+        slot = 0 if 0 not in st.pending.values() else 1
+        st.pending = {m: v for m, v in st.pending.items() if v != slot}
+        _decode_block(module, st.buffer(slot, _n_elements(module)), tpb, bpt)
+    # Views: injected when the block's weights do not already view this buffer.
+    views = (slot, st.bufs[slot].data_ptr())
+    if module.__dict__.get("_ecf8_pf_views") != views:
+        inject_weights(module, st.buffer(slot, _n_elements(module)))
+        module.__dict__["_ecf8_pf_views"] = views
     # The next block goes into the other buffer once everything enqueued so far
     # on this stream is done (that buffer was read by the block before this one).
     other = 1 - slot
-    st.pending = {m: v for m, v in st.pending.items() if v[0] != other}
-    nbuf = st.buffer(other, _n_elements(nxt))
-    done = torch.cuda.Event()
-    done.record(cur)
-    st.side.wait_event(done)
-    with torch.cuda.stream(st.side):
-        _, fresh = _block_table(nxt)
-        decode_stream(nxt.luts, nxt.encoded, nxt.packed_other_4bits, nxt.output_positions, nxt.gaps, nbuf,
-                      tpb, bpt, table=nxt.ecf8_decode_table, stream=st.side)
-        ready = torch.cuda.Event()
-        ready.record(st.side)
-    st.pending[nxt] = (other, ready)
+    st.pending = {m: v for m, v in st.pending.items() if v != other}
+    _block_table(nxt)  # built on this stream at first use, before the side stream waits for it
+    st.done.record(cur)
+    st.side.wait_event(st.done)
+    _prefetch_launch(st, nxt, other, tpb, bpt, module.__dict__.get("_ecf8_prefetch_ctas", 0))
+    st.ready[other].record(st.side)
+    st.pending[nxt] = other
 
 
 def _prefetch_blocks(module):
     return getattr(module, "_ecf8_blocks", None) or [module]
 
 
-def enable_decode_prefetch(model, enable=True):
+def enable_decode_prefetch(model, enable=True, ctas=0):
     """Decode-ahead mode of the forward-pre-hook: each hooked block, in module
     order (the forward order of decoder layers and DiT blocks), starts the
     next block's decode on a side stream into the second of two per-device
@@ -432,15 +456,24 @@ def enable_decode_prefetch(model, enable=True):
     while it runs, so it does not share them with the block's own kernels,
     and the mode costs some host time per block (the batch-16 Qwen3-8B
     generation of the benchmark, whose step keeps the GPU busy, runs slower
-    with it: 0.838 against 0.889 of the uncompressed tokens/s).  Uses two scratch buffers of the largest block
-    instead of one.  The last block prefetches the first (the next forward).
-    Returns the number of hooked blocks.  enable=False restores the plain hook."""
+    with it: 0.918 against 0.948 of the uncompressed tokens/s).  `ctas` > 0
+    limits the side-stream decodes to that many CTAs (of one per SM), so they
+    take only part of the GPU and the block's own kernels keep the rest (on
+    that generation: 0.913 with 32 CTAs, 0.904 with 74).  Uses
+    two scratch buffers of the largest block instead of one.  The last block
+    prefetches the first (the next forward).  Returns the number of hooked
+    blocks.  enable=False restores the plain hook."""
     blocks = [m for m in model.modules() if "encoded" in m._buffers and "luts" in m._buffers
               and any(getattr(h, "__name__", "") == "decode_hook" for h in m._forward_pre_hooks.values())]
     for i, m in enumerate(blocks):
         # plain attributes: assigning a module through nn.Module would make it a child
         object.__setattr__(m, "_ecf8_next", blocks[(i + 1) % len(blocks)] if enable else None)
         object.__setattr__(m, "_ecf8_blocks", blocks if enable else None)
+        object.__setattr__(m, "_ecf8_prefetch_ctas", int(ctas) if enable else 0)
+        # Either hook's kept launch state assumes the weights view its own
+        # buffers: switching modes re-injects the views on the next decode.
+        for k in ("_ecf8_launch", "_ecf8_pf_views", "_ecf8_pf_launch"):
+            m.__dict__.pop(k, None)
     if not enable:
         _PREFETCH.clear()
     return len(blocks)

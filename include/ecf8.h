@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define ECF8_ABI_VERSION 7
+#define ECF8_ABI_VERSION 8
 
 /* Status codes. */
 #define ECF8_OK 0
@@ -122,7 +122,8 @@ int ecf8_decode_batch(const ecf8_stream* streams, int n_streams,
 /*
  * ecf8_decode_batch with flags.  flags = 0 behaves exactly like
  * ecf8_decode_batch; other bits than the ones below are rejected
- * (ECF8_ERR_INVALID_ARGUMENT).
+ * (ECF8_ERR_INVALID_ARGUMENT).  Neither option has a counterpart in the
+ * reference (whose launches are plain stream-ordered kernels).
  *
  * ECF8_DECODE_OVERLAP_PREVIOUS: launches with programmatic dependent launch.
  * The decode may start while the previous kernel on cuda_stream is still
@@ -132,10 +133,16 @@ int ecf8_decode_batch(const ecf8_stream* streams, int n_streams,
  * (one per layer) then overlap one launch's set-up with the previous one's
  * last groups.  The caller guarantees that no work still in flight on the
  * stream writes the inputs; work writing or reading the outputs is ordered
- * as without the flag.  Has no counterpart in the reference (whose launches
- * are plain stream-ordered kernels).
+ * as without the flag.
+ *
+ * ECF8_DECODE_CTAS(n), n in 1..65535 (bits 31..16): launches at most n CTAs
+ * instead of one per SM; every CTA still holds a whole SM's worth of shared
+ * memory.  A decode issued ahead of use on a second CUDA stream then leaves
+ * the other SMs to the kernels of the first.  The output is the same.
  */
 #define ECF8_DECODE_OVERLAP_PREVIOUS 1u
+#define ECF8_DECODE_CTAS_SHIFT 16
+#define ECF8_DECODE_CTAS(n) ((uint32_t)(n) << ECF8_DECODE_CTAS_SHIFT)
 int ecf8_decode_batch_flags(const ecf8_stream* streams, int n_streams,
                             int threads_per_block, int bytes_per_thread,
                             uint32_t flags, void* cuda_stream);

@@ -38,7 +38,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_abi_version_and_status_strings(lib):
-    assert lib.ecf8_abi_version() == 7
+    assert lib.ecf8_abi_version() == 8
     assert lib.ecf8_status_string(0) == b"ok"
     assert b"invalid" in lib.ecf8_status_string(1)
     assert lib.ecf8_last_cuda_error() == 0
@@ -101,9 +101,14 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
 
 
 def test_decode_batch_flags_rejects_unknown_flags(lib):
-    """Unknown flag bits are refused before anything touches a device."""
+    """Unknown flag bits are refused before anything touches a device; the
+    CTA limit (bits 31..16) is accepted."""
     from ecf8_b200 import _lib
     assert lib.ecf8_decode_batch_flags(None, 0, 512, 8, 2, None) == _lib.ERR_INVALID_ARGUMENT
-    assert lib.ecf8_decode_batch_flags(None, 0, 512, 8, 0x80000000, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.ecf8_decode_batch_flags(None, 0, 512, 8, 0x8000, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.ecf8_decode_batch_flags(None, 0, 512, 8, _lib.decode_ctas(32) | 4, None) == _lib.ERR_INVALID_ARGUMENT
+    assert lib.ecf8_decode_batch_flags(None, 0, 512, 8, _lib.decode_ctas(65535), None) == _lib.OK
+    assert lib.ecf8_decode_batch_flags(None, 0, 512, 8, _lib.decode_ctas(1) | _lib.DECODE_OVERLAP_PREVIOUS,
+                                       None) == _lib.OK
     assert lib.ecf8_decode_batch_flags(None, 0, 256, 8, _lib.DECODE_OVERLAP_PREVIOUS, None) == _lib.ERR_UNSUPPORTED
     assert lib.ecf8_decode_batch_flags(None, 0, 512, 8, _lib.DECODE_OVERLAP_PREVIOUS, None) == _lib.OK

@@ -156,6 +156,39 @@ def test_batch_larger_than_one_launch(cuda_device, oracle_mod, overlap):
         assert np.array_equal(o.cpu().numpy(), s["fp8"])
 
 
+@pytest.mark.parametrize("ctas", [1, 3, 37])
+def test_decode_with_fewer_ctas(cuda_device, oracle_mod, ctas):
+    """ECF8_DECODE_CTAS(n): a launch of n CTAs (each covering more groups and
+    more stream boundaries) gives the same bytes, with and without launch
+    overlap, for a multi-stream batch and for a stream larger than the grid's
+    share of work."""
+    from ecf8_b200 import _lib
+    from ecf8_b200.run import _stream_struct, build_decode_table, decode_stream
+    rng = np.random.default_rng(ctas)
+    ss = [random_stream(oracle_mod, rng, n=int(rng.integers(1, 4000)) * 2) for _ in range(9)]
+    ss += [load_golden(n) for n in golden_names()[:4]]
+    ds = [to_device(s, cuda_device) for s in ss]
+    outs = [torch.full((s["fp8"].size,), GUARD, dtype=torch.uint8, device=cuda_device) for s in ss]
+    for d in ds:
+        d["decode_table"] = build_decode_table(d["luts"])
+    arr = (_lib.Ecf8Stream * len(ds))(*[_stream_struct(d, o, d["decode_table"]) for d, o in zip(ds, outs)])
+    L = _lib.lib()
+    for flags in (_lib.decode_ctas(ctas), _lib.decode_ctas(ctas) | _lib.DECODE_OVERLAP_PREVIOUS):
+        for o in outs:
+            o.fill_(GUARD)
+        st = L.ecf8_decode_batch_flags(arr, len(ds), 512, 8, flags, torch.cuda.current_stream().cuda_stream)
+        assert st == _lib.OK
+        torch.cuda.synchronize()
+        for s, o in zip(ss, outs):
+            assert np.array_equal(o.cpu().numpy(), s["fp8"])
+    big = random_stream(oracle_mod, rng, n=400_000)
+    d = to_device(big, cuda_device)
+    out = decode_stream(d["luts"], d["encoded"], d["packed_other_4bits"], d["output_positions"], d["gaps"],
+                        max_ctas=ctas)
+    torch.cuda.synchronize()
+    assert np.array_equal(out.view(torch.uint8).cpu().numpy(), big["fp8"])
+
+
 def test_reference_call_convention(cuda_device):
     """`_decode(grid=, block=, shared_mem=, args=[...])` as compress.py:109-124 calls it."""
     from ecf8_b200 import _decode

@@ -166,7 +166,9 @@ def test_reference_launcher_caches_tables_and_survives_reused_lut_memory(cuda_de
 def test_decode_prefetch_mode_matches_uncompressed(cuda_device, tmp_path):
     """enable_decode_prefetch: each block's hook decodes the next block on a
     side stream into the second scratch buffer; outputs stay bit-identical
-    over repeated forwards, and turning it off restores the plain hook."""
+    over repeated forwards (also with the side-stream decodes limited to a
+    few CTAs), and switching from the plain hook and back to it re-points the
+    weights each time."""
     from ecf8_b200 import enable_decode_prefetch, load_and_replace_tensors
     from ecf8_b200.run import TensorManager
     dev = cuda_device
@@ -181,6 +183,8 @@ def test_decode_prefetch_mode_matches_uncompressed(cuda_device, tmp_path):
     model.to(dev)
     TensorManager.clear_device()
     keys = list(model.state_dict())
+    assert torch.equal(model(x), y_ref)  # plain hook first: plain -> prefetch -> plain below
+    assert torch.equal(model(x), y_ref)
     assert enable_decode_prefetch(model) == 4
     assert list(model.state_dict()) == keys  # the block chain is not part of the module tree
     for _ in range(4):
@@ -188,5 +192,9 @@ def test_decode_prefetch_mode_matches_uncompressed(cuda_device, tmp_path):
     # the blocks alternate between two buffers
     ptrs = [blk.down_proj.weight.data_ptr() for blk in model.layers]
     assert len(set(ptrs)) == 2
+    # side-stream decodes limited to a few CTAs: the same bytes
+    assert enable_decode_prefetch(model, ctas=5) == 4
+    for _ in range(3):
+        assert torch.equal(model(x), y_ref)
     enable_decode_prefetch(model, enable=False)
     assert torch.equal(model(x), y_ref)
