@@ -27,7 +27,6 @@ identical decoded weights must give identical logits.
 
 import argparse
 import json
-import sys
 import time
 
 import torch

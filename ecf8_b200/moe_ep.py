@@ -18,7 +18,6 @@ expert index.  Linear weights are e4m3 with 128x128 block scales
 (ecf8_b200.fp8_model.Fp8Linear); router, norms, embeddings and lm_head bf16.
 """
 
-import math
 from dataclasses import dataclass
 
 import torch

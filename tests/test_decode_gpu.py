@@ -2,7 +2,6 @@
 original bytes, the CPU oracle and the reference kernel decode.cu compiled
 unmodified for sm_100a, on the reference's own golden streams, adversarial
 streams and random streams."""
-import ctypes
 import hashlib
 import json
 import math
