@@ -3,7 +3,7 @@ import numpy as np
 import pytest
 
 from conftest import golden_names, load_golden
-from helpers import random_stream, table_to_arrays
+from helpers import random_stream
 
 
 def table_from_golden(s):

@@ -1,6 +1,5 @@
 """Compressor host logic (CPU): block discovery by the family patterns, the
 reference's layer-finding helpers, and the FP8 model assembly it reads."""
-import os
 
 import pytest
 import torch
